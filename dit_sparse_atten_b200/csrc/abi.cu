@@ -1,0 +1,322 @@
+// C ABI of libbsa.so (declared in include/bsa.h): argument validation, TMA
+// tensor-map encoding and kernel launch.  No entry point allocates memory or
+// synchronises the stream.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/bsa.h"
+#include "bsa_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(BSA_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int ok() {
+  g_last_error.clear();
+  return BSA_OK;
+}
+
+int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4-D bf16 tensor map over a [B, T, H, D] tensor with element strides
+// (sb, st, sh), D contiguous.  Box: 64 features x `rows` tokens x 1 head x 1
+// batch, 128-byte swizzle, zero fill out of bounds.  Dimensions are ordered by
+// increasing stride: (D, H, T, B) when sh <= st, else (D, T, H, B); `t_major`
+// reports the second case (coordinate order (d, t, h, b)).
+int encode_bhtd(CUtensorMap* map, const void* ptr, int64_t B, int64_t T, int64_t H, int64_t D,
+                int64_t sb, int64_t st, int64_t sh, int rows, bool* t_major) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(BSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "tensor base address must be 16-byte aligned");
+  if (((sb * 2) & 15) || ((st * 2) & 15) || ((sh * 2) & 15))
+    return fail(BSA_ERR_INVALID_ARGUMENT,
+                "token/head/batch strides must be multiples of 8 elements (16 bytes)");
+  *t_major = st < sh;
+  cuuint64_t dims[4], strides[3];
+  dims[0] = static_cast<cuuint64_t>(D);
+  if (!*t_major) {
+    dims[1] = H; dims[2] = T;
+    strides[0] = sh * 2; strides[1] = st * 2;
+  } else {
+    dims[1] = T; dims[2] = H;
+    strides[0] = st * 2; strides[1] = sh * 2;
+  }
+  dims[3] = B;
+  strides[2] = sb * 2;
+  if (B == 1) strides[2] = strides[1] * dims[2];  // unused; keep it well-formed
+  cuuint32_t box[4] = {64u, 1u, static_cast<cuuint32_t>(rows), 1u};
+  if (*t_major) { box[1] = static_cast<cuuint32_t>(rows); box[2] = 1u; }
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BSA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return BSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bsa_version(void) { return 10000; }
+
+const char* bsa_last_error(void) { return g_last_error.c_str(); }
+
+int bsa_reorder_rows(int32_t n_tensors, const void* const* src, void* const* dst,
+                     const int32_t* perm, int64_t batch, int64_t tokens_out, int64_t tokens_in,
+                     int64_t row_bytes, int32_t* err_word, void* stream) {
+  if (n_tensors < 1 || n_tensors > 3)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "n_tensors must be 1, 2 or 3");
+  if (src == nullptr || dst == nullptr || perm == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  for (int t = 0; t < n_tensors; ++t)
+    if (src[t] == nullptr || dst[t] == nullptr)
+      return fail(BSA_ERR_INVALID_ARGUMENT, "null tensor pointer %d", t);
+  if (batch < 0 || tokens_out < 0 || tokens_in < 0 || row_bytes <= 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "negative size or empty row");
+  cudaError_t e = bsa::launch_reorder_rows(n_tensors, src, dst, perm, batch, tokens_out,
+                                           tokens_in, row_bytes, err_word,
+                                           static_cast<cudaStream_t>(stream), sm_count());
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_reorder_rows launch");
+  return ok();
+}
+
+int bsa_pack_boolean_rows(const uint8_t* route, int64_t rows, int32_t cols, int32_t* counts,
+                          int32_t* indices, void* stream) {
+  if (route == nullptr || counts == nullptr || indices == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (rows < 0 || cols <= 0 || cols > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "cols must be in [1, 4096] (got %d)", cols);
+  bsa::SelectArgs a{};
+  a.route_in = route;
+  a.rows = rows;
+  a.cols = cols;
+  a.rows_per_group = 1;
+  a.counts = counts;
+  a.indices = indices;
+  cudaError_t e = bsa::launch_route_select(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_pack_boolean_rows launch");
+  return ok();
+}
+
+int bsa_route_select(const float* mass, const uint8_t* prev, int64_t rows, int32_t cols,
+                     int32_t rows_per_group, float persistence, float target,
+                     int32_t max_blocks, int32_t sink_blocks, uint8_t* route_out,
+                     int32_t* counts, int32_t* indices, uint64_t* kept, void* stream) {
+  if (mass == nullptr) return fail(BSA_ERR_INVALID_ARGUMENT, "mass is null");
+  if (rows < 0 || cols <= 0 || cols > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "cols must be in [1, 4096] (got %d)", cols);
+  if (max_blocks < 1 || max_blocks > cols)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "max_blocks must be in [1, cols] (got %d)", max_blocks);
+  if (!(target > 0.f && target <= 1.f))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "mass_target must be in (0, 1]");
+  if (persistence < 0.f) return fail(BSA_ERR_INVALID_ARGUMENT, "persistence must be >= 0");
+  if (kept != nullptr && (rows_per_group <= 0 || rows % rows_per_group != 0))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "rows must be a multiple of rows_per_group");
+  bsa::SelectArgs a{};
+  a.mass = mass;
+  a.prev = prev;
+  a.persistence = persistence;
+  a.target = target;
+  a.cap = max_blocks;
+  a.sink_blocks = sink_blocks < 0 ? 0 : sink_blocks;
+  a.rows = rows;
+  a.cols = cols;
+  a.rows_per_group = rows_per_group > 0 ? rows_per_group : 1;
+  a.route_out = route_out;
+  a.counts = counts;
+  a.indices = indices;
+  a.kept = reinterpret_cast<unsigned long long*>(kept);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kept != nullptr) {
+    cudaError_t e = cudaMemsetAsync(kept, 0, sizeof(uint64_t) * (rows / a.rows_per_group), s);
+    if (e != cudaSuccess) return cuda_fail(e, "bsa_route_select memset");
+  }
+  cudaError_t e = bsa::launch_route_select(a, s);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_route_select launch");
+  return ok();
+}
+
+int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch, int64_t heads,
+                     int32_t q_blocks, int32_t samples, int32_t head_dim,
+                     const float* block_bias, float scale, int32_t round_bf16, float* mass,
+                     int32_t* err_word, void* stream) {
+  if (sampled_q == nullptr || sampled_k == nullptr || block_bias == nullptr || mass == nullptr ||
+      err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (samples != 1 && samples != 2 && samples != 4 && samples != 8 && samples != 16 &&
+      samples != 32)
+    return fail(BSA_ERR_UNSUPPORTED, "samples must be a power of two <= 32 (got %d)", samples);
+  if (q_blocks <= 0 || q_blocks > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "q_blocks must be in [1, 4096] (got %d)", q_blocks);
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/heads");
+  const int64_t n_rows = static_cast<int64_t>(q_blocks) * samples;
+  CUtensorMap tq, tk;
+  bool tm = false;
+  int rc = encode_bhtd(&tq, sampled_q, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
+                       heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  rc = encode_bhtd(&tk, sampled_k, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
+                   heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  if (tm) return fail(BSA_ERR_INVALID_ARGUMENT, "sampled tensors must be [B, N, H, D] contiguous");
+  bsa::MassArgs a{};
+  a.batch = batch;
+  a.heads = heads;
+  a.n_rows = n_rows;
+  a.samples = samples;
+  a.q_blocks = q_blocks;
+  a.scale = scale;
+  a.round_bf16 = round_bf16;
+  a.block_bias = block_bias;
+  a.mass_scale = 1.0f / static_cast<float>(samples);
+  a.mass = mass;
+  a.err_word = err_word;
+  cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass launch");
+  return ok();
+}
+
+int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t tokens,
+                         int64_t heads, int32_t head_dim, int32_t block, float scale, float* mass,
+                         int32_t* err_word, void* stream) {
+  if (q == nullptr || k == nullptr || mass == nullptr || err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (block != 32 && block != 64 && block != 128)
+    return fail(BSA_ERR_UNSUPPORTED, "block must be 32, 64 or 128 (got %d)", block);
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/tokens/heads");
+  const int64_t blocks = (tokens + block - 1) / block;
+  if (blocks > 4096) return fail(BSA_ERR_UNSUPPORTED, "at most 4096 blocks (got %lld)",
+                                 static_cast<long long>(blocks));
+  CUtensorMap tq, tk;
+  bool tm = false;
+  int rc = encode_bhtd(&tq, q, batch, tokens, heads, head_dim, tokens * heads * head_dim,
+                       heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  rc = encode_bhtd(&tk, k, batch, tokens, heads, head_dim, tokens * heads * head_dim,
+                   heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  bsa::MassArgs a{};
+  a.batch = batch;
+  a.heads = heads;
+  a.n_rows = tokens;
+  a.samples = block;
+  a.q_blocks = static_cast<int32_t>(blocks);
+  a.scale = scale;
+  a.round_bf16 = 0;
+  a.block_bias = nullptr;
+  a.mass_scale = 1.0f;
+  a.mass = mass;
+  a.err_word = err_word;
+  cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_exact_block_mass launch");
+  return ok();
+}
+
+int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
+                      int64_t heads, int32_t head_dim, int64_t in_stride_b, int64_t in_stride_t,
+                      int64_t in_stride_h, const int32_t* counts, const int32_t* indices,
+                      int32_t route_cols, int32_t route_has_batch, int32_t block, float scale,
+                      void* out, int64_t out_stride_b, int64_t out_stride_t,
+                      int64_t out_stride_h, float* lse, int32_t* err_word, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || counts == nullptr ||
+      indices == nullptr || err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (block != 64 && block != 128)
+    return fail(BSA_ERR_UNSUPPORTED, "block must be 64 or 128 (got %d)", block);
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/tokens/heads");
+  const int64_t qblocks = (tokens + block - 1) / block;
+  if (qblocks > 0x7fffffff) return fail(BSA_ERR_UNSUPPORTED, "too many blocks");
+  if (route_cols < qblocks)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "route_cols (%d) < key blocks (%lld)", route_cols,
+                static_cast<long long>(qblocks));
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || ((out_stride_t * 2) & 15) ||
+      ((out_stride_h * 2) & 15) || ((out_stride_b * 2) & 15))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "out must be 16-byte aligned with 16-byte strides");
+  CUtensorMap tq, tk, tv;
+  bool tmq = false, tmk = false, tmv = false;
+  int rc = encode_bhtd(&tq, q, batch, tokens, heads, head_dim, in_stride_b, in_stride_t,
+                       in_stride_h, block, &tmq);
+  if (rc != BSA_OK) return rc;
+  rc = encode_bhtd(&tk, k, batch, tokens, heads, head_dim, in_stride_b, in_stride_t, in_stride_h,
+                   block, &tmk);
+  if (rc != BSA_OK) return rc;
+  rc = encode_bhtd(&tv, v, batch, tokens, heads, head_dim, in_stride_b, in_stride_t, in_stride_h,
+                   block, &tmv);
+  if (rc != BSA_OK) return rc;
+  if (tmq) return fail(BSA_ERR_UNSUPPORTED, "token stride below head stride is not supported");
+  bsa::AttnArgs a{};
+  a.batch = batch;
+  a.tokens = tokens;
+  a.heads = heads;
+  a.q_blocks = static_cast<int32_t>(qblocks);
+  a.k_blocks = static_cast<int32_t>(qblocks);
+  a.block = block;
+  a.route_cols = route_cols;
+  a.route_batch_stride = route_has_batch ? 1 : 0;
+  a.counts = counts;
+  a.indices = indices;
+  a.scale = scale;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.out_stride_b = out_stride_b;
+  a.out_stride_t = out_stride_t;
+  a.out_stride_h = out_stride_h;
+  a.lse = lse;
+  a.err_word = err_word;
+  cudaError_t e = bsa::launch_attention(tq, tk, tv, a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_attention_fwd launch");
+  return ok();
+}
+
+}  // extern "C"

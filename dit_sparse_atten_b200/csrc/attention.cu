@@ -1,0 +1,387 @@
+// (a) Block-sparse flash attention over a per-[batch, head, query-block] CSR
+// route, for sm_100a.
+//
+// Reference semantics: FlexAttention with full blocks only, as driven by
+// attention_backends/flex.py:308-355 (route -> BlockMask) and :379-399
+// (padding, kernel call, trim); equivalently the gather/softmax/PV of
+// attention_backends/sparse.py:670-751.  A query in block qb of head h attends
+// to every valid key (< T) in the key blocks listed in its CSR row.
+//
+// One CTA handles one (qb, h, b) work item: 128 query rows (the MMA M), key
+// blocks of BK = 128 (or 64) tokens.
+//   warp 4      TMA producer: Q once, then K/V tiles by routed block id into a
+//               ring of shared-memory slots (consumption order K0,K1,V0,K2,V1..)
+//   warp 5      TMEM allocator and single-thread tcgen05.mma issuer:
+//               S_j = Q K_j^T into one of two TMEM S buffers, O += P_j V_j
+//   warps 0-3   softmax: thread i owns query row i (TMEM lane i); reads S_j,
+//               online max/sum in the log2 domain, writes bf16 P_j to shared
+//               memory (128-byte swizzle), rescales O in TMEM when the running
+//               max grows by more than 2^8, and runs the epilogue.
+// TMEM columns: S buffers at [0,BK) and [128,128+BK), O at [256,384).
+// Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
+// kErrWaitTimeout in the caller's error word, drains its in-flight copies and
+// MMAs, frees TMEM and exits.
+#include "bsa_kernels.h"
+
+namespace bsa {
+namespace {
+
+constexpr int kAttnThreads = 192;
+constexpr int kHeadDim = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+template <int BK>
+struct AttnLayout {
+  static constexpr int kPanelRows = 128;                 // Q / P panels always 128 rows
+  static constexpr int kQBytes = 2 * kPanelRows * 128;   // two 64-column panels
+  static constexpr int kSlotPanel = BK * 128;            // one 64-column panel of K or V
+  static constexpr int kSlotBytes = 2 * kSlotPanel;
+  static constexpr int kPBytes = (BK / 64) * kPanelRows * 128;
+  static constexpr int kSlots = BK == 128 ? 5 : 8;
+  static constexpr int kQOff = 0;
+  static constexpr int kRingOff = kQOff + kQBytes;
+  static constexpr int kPOff = kRingOff + kSlots * kSlotBytes;
+  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;  // + alignment slack
+};
+
+struct AttnBarriers {
+  uint64_t q_full;
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t o_done;
+  uint64_t drain;
+  uint64_t slot_full[8];
+  uint64_t slot_empty[8];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int BK>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    bsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
+  using L = AttnLayout<BK>;
+  static_assert(sizeof(AttnBarriers) <= L::kBarBytes, "barrier area");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem + L::kQOff;
+  uint8_t* sRing = smem + L::kRingOff;
+  uint8_t* sP = smem + L::kPOff;
+  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(smem + L::kBarOff);
+  volatile int* abort_flag = &bar->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int64_t rb = a.route_batch_stride ? b : 0;
+  const int64_t route_row = (rb * a.heads + h) * a.q_blocks + qb;
+  const int32_t* kv_list = a.indices + route_row * a.route_cols;
+  int n = a.counts[route_row];
+  if (n < 0 || n > a.route_cols || n > a.k_blocks) {
+    if (threadIdx.x == 0) atomicOr(a.err_word, kErrBadRoute);
+    n = n < 0 ? 0 : min(n, min(a.route_cols, a.k_blocks));
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->s_full[0], 1);
+    mbar_init(&bar->s_full[1], 1);
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->o_done, 1);
+    mbar_init(&bar->drain, 1);
+    for (int s = 0; s < L::kSlots; ++s) {
+      mbar_init(&bar->slot_full[s], 1);
+      mbar_init(&bar->slot_empty[s], 1);
+    }
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (BK == 64 && threadIdx.x < 128) {
+    // Rows 64..127 of the Q panels are never loaded; keep them finite.
+    uint4 zero = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < 2 * 64 * 8; i += 128) {
+      const int panel = i / (64 * 8);
+      const int off = i % (64 * 8);
+      reinterpret_cast<uint4*>(sQ + panel * L::kPanelRows * 128 + 64 * 128)[off] = zero;
+    }
+    fence_proxy_async_smem();
+  }
+  if (warp == 5) tmem_alloc(&bar->tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+
+  auto block_id = [&](int j) -> int {
+    int kb = __ldg(kv_list + j);
+    if (kb < 0 || kb >= a.k_blocks) {
+      atomicOr(a.err_word, kErrBadRoute);
+      kb = kb < 0 ? 0 : a.k_blocks - 1;
+    }
+    return kb;
+  };
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(&bar->q_full, 2 * BK * 128);
+      tma_load_4d(sQ, &tm_q, &bar->q_full, 0, h, qb * BK, b);
+      tma_load_4d(sQ + L::kPanelRows * 128, &tm_q, &bar->q_full, 64, h, qb * BK, b);
+      uint32_t armed[L::kSlots];
+      int seq = 0;
+      bool ok = true;
+      auto load = [&](const CUtensorMap* tm, int kb) {
+        const int s = seq % L::kSlots;
+        const uint32_t ph = (seq / L::kSlots) & 1;
+        if (!mbar_wait(&bar->slot_empty[s], ph ^ 1, abort_flag, a.err_word)) return false;
+        uint8_t* dst = sRing + s * L::kSlotBytes;
+        mbar_arrive_expect_tx(&bar->slot_full[s], L::kSlotBytes);
+        tma_load_4d(dst, tm, &bar->slot_full[s], 0, h, kb * BK, b);
+        tma_load_4d(dst + L::kSlotPanel, tm, &bar->slot_full[s], 64, h, kb * BK, b);
+        armed[s] = ph;
+        ++seq;
+        return true;
+      };
+      for (int s = 0; s < L::kSlots; ++s) armed[s] = 2;
+      ok = load(&tm_k, block_id(0));
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) ok = load(&tm_k, block_id(j + 1));
+        if (ok) ok = load(&tm_v, block_id(j));
+      }
+      // Never leave a copy in flight into shared memory.
+      int never = 0;
+      mbar_wait(&bar->q_full, 0, &never, a.err_word);
+      for (int s = 0; s < L::kSlots; ++s)
+        if (armed[s] < 2) mbar_wait(&bar->slot_full[s], armed[s], &never, a.err_word);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n > 0) {
+      const uint32_t idesc_s = idesc_bf16_f32(128, BK, false);
+      const uint32_t idesc_o = idesc_bf16_f32(128, kHeadDim, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      const uint32_t ring_addr = smem_u32(sRing);
+      int seq = 0;
+      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
+      auto issue_s = [&](int j) {
+        const int s = seq % L::kSlots;
+        const uint32_t ph = (seq / L::kSlots) & 1;
+        if (!mbar_wait(&bar->slot_full[s], ph, abort_flag, a.err_word)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = ring_addr + s * L::kSlotBytes;
+        const uint32_t d = tmem + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          const uint64_t da = sdesc_sw128(q_addr + (kk >> 2) * (L::kPanelRows * 128) + off, 16, 1024);
+          const uint64_t db = sdesc_sw128(k_addr + (kk >> 2) * L::kSlotPanel + off, 16, 1024);
+          umma_bf16_ss(d, da, db, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar->s_full[j & 1]);
+        umma_commit(&bar->slot_empty[s]);
+        ++seq;
+        return true;
+      };
+      auto issue_pv = [&](int j) {
+        const int s = seq % L::kSlots;
+        const uint32_t ph = (seq / L::kSlots) & 1;
+        if (!mbar_wait(&bar->slot_full[s], ph, abort_flag, a.err_word)) return false;
+        if (!mbar_wait(&bar->p_full, j & 1, abort_flag, a.err_word)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = ring_addr + s * L::kSlotBytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t da = sdesc_sw128(p_addr + (kk >> 2) * (L::kPanelRows * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = sdesc_sw128(v_addr + kk * 16 * 128, L::kSlotPanel, 1024);
+          umma_bf16_ss(tmem + 256, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bar->slot_empty[s]);
+        umma_commit(&bar->o_done);
+        ++seq;
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) ok = issue_s(j + 1);
+        if (ok) ok = issue_pv(j);
+      }
+      // Wait for every issued MMA before TMEM is released.
+      int never = 0;
+      umma_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0, &never, a.err_word);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int row = threadIdx.x;  // 0..127 == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    const bool warp_active = (BK == 128) || (warp < 2);
+    const int64_t token = static_cast<int64_t>(qb) * BK + row;
+    const bool row_valid = warp_active && row < BK && token < a.tokens;
+    const float c = a.scale * kLog2e;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; ok && j < n; ++j) {
+      ok = mbar_wait(&bar->s_full[j & 1], (j >> 1) & 1, abort_flag, a.err_word);
+      if (!ok) break;
+      tc_fence_after();
+      float s[BK];
+      float p_scale = 1.f;
+      bool need = false;
+      if (warp_active) {
+        uint32_t r[BK];
+#pragma unroll
+        for (int cchunk = 0; cchunk < BK / 32; ++cchunk)
+          tmem_ld_32x32b_x32(tmem + lane_addr + (j & 1) * 128 + cchunk * 32, r + cchunk * 32);
+        tmem_wait_ld();
+        reg_fence<BK>(r);
+#pragma unroll
+        for (int x = 0; x < BK; ++x) s[x] = __uint_as_float(r[x]);
+        const int kb = block_id(j);
+        const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
+        if (valid < BK) {
+#pragma unroll
+          for (int x = 0; x < BK; ++x)
+            if (x >= valid) s[x] = -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int x = 1; x < BK; ++x) mx = fmaxf(mx, s[x]);
+        const float mrow = mx * c;
+        need = mrow > m_used + kRescaleThreshold;
+        const float m_new = need ? mrow : m_used;
+        p_scale = need ? ex2_approx(m_used - m_new) : 1.f;
+        m_used = m_new;
+        l *= p_scale;
+        float rs = 0.f;
+#pragma unroll
+        for (int x = 0; x < BK; ++x) {
+          s[x] = ex2_approx(fmaf(s[x], c, -m_used));
+          rs += s[x];
+        }
+        l += rs;
+      }
+      // PV_{j-1} must be complete before P is overwritten or O rescaled.
+      if (j > 0) {
+        ok = mbar_wait(&bar->o_done, (j - 1) & 1, abort_flag, a.err_word);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (warp_active) {
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int cchunk = 0; cchunk < kHeadDim / 32; ++cchunk) {
+            uint32_t o[32];
+            const uint32_t addr = tmem + lane_addr + 256 + cchunk * 32;
+            tmem_ld_32x32b_x32(addr, o);
+            tmem_wait_ld();
+            reg_fence<32>(o);
+#pragma unroll
+            for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * p_scale);
+            tmem_st_32x32b_x32(addr, o);
+            tmem_wait_st();
+          }
+        }
+#pragma unroll
+        for (int ch = 0; ch < BK / 8; ++ch) {
+          uint4 pk;
+          pk.x = pack_bf16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
+          pk.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
+          pk.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
+          pk.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
+          uint8_t* dst = sP + (ch >> 3) * (L::kPanelRows * 128) + sw128_offset(row, ch & 7);
+          *reinterpret_cast<uint4*>(dst) = pk;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    // ---------------------------------------------------------- epilogue
+    if (ok && n > 0) {
+      ok = mbar_wait(&bar->o_done, (n - 1) & 1, abort_flag, a.err_word);
+      tc_fence_after();
+    }
+    if (warp_active) {
+      __nv_bfloat16* out = a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h;
+      const float inv_l = (n > 0 && l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll
+      for (int cchunk = 0; cchunk < kHeadDim / 32; ++cchunk) {
+        uint32_t o[32];
+        if (ok && n > 0) {
+          tmem_ld_32x32b_x32(tmem + lane_addr + 256 + cchunk * 32, o);
+          tmem_wait_ld();
+          reg_fence<32>(o);
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) o[x] = 0u;
+        }
+        if (row_valid) {
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * inv_l, __uint_as_float(o[v4 * 8 + 1]) * inv_l);
+            pk.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * inv_l, __uint_as_float(o[v4 * 8 + 3]) * inv_l);
+            pk.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * inv_l, __uint_as_float(o[v4 * 8 + 5]) * inv_l);
+            pk.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * inv_l, __uint_as_float(o[v4 * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(out + cchunk * 32 + v4 * 8) = pk;
+          }
+        }
+      }
+      if (row_valid && a.lse != nullptr) {
+        a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
+            (n > 0 && l > 0.f) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int BK>
+cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                      const AttnArgs& a, cudaStream_t stream) {
+  using L = AttnLayout<BK>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(bsa_attention_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             L::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const dim3 grid(static_cast<unsigned>(a.q_blocks), static_cast<unsigned>(a.heads),
+                  static_cast<unsigned>(a.batch));
+  bsa_attention_kernel<BK><<<grid, kAttnThreads, L::kSmemBytes, stream>>>(tq, tk, tv, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const AttnArgs& a, cudaStream_t stream) {
+  if (a.batch == 0 || a.heads == 0 || a.q_blocks == 0) return cudaSuccess;
+  if (a.block == 128) return launch_bk<128>(tq, tk, tv, a, stream);
+  if (a.block == 64) return launch_bk<64>(tq, tk, tv, a, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace bsa

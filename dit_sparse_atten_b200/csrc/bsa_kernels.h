@@ -1,0 +1,71 @@
+// Internal launcher declarations shared by the kernel translation units and the
+// C ABI (abi.cu).  Not part of the public interface (include/bsa.h is).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bsa_common.cuh"
+
+namespace bsa {
+
+// ---- (c) reorder ----------------------------------------------------------
+cudaError_t launch_reorder_rows(int n_tensors, const void* const* src, void* const* dst,
+                                const int32_t* perm, int64_t batch, int64_t tokens_out,
+                                int64_t tokens_in, int64_t row_bytes, int* err_word,
+                                cudaStream_t stream, int num_sms);
+
+// ---- (b) route selection / CSR pack ----------------------------------------
+struct SelectArgs {
+  const float* mass;        // [rows, cols] fp32, or nullptr for a pure pack
+  const uint8_t* prev;      // [rows, cols] 0/1, or nullptr
+  const uint8_t* route_in;  // [rows, cols] 0/1 when packing an existing route
+  float persistence;
+  float target;
+  int32_t cap;              // max(1, ceil(cols * keep))
+  int32_t sink_blocks;
+  int64_t rows;
+  int32_t cols;
+  int32_t rows_per_group;   // rows that share one kept counter (Qb)
+  uint8_t* route_out;       // [rows, cols] or nullptr
+  int32_t* counts;          // [rows] or nullptr
+  int32_t* indices;         // [rows, cols] or nullptr
+  unsigned long long* kept; // [rows / rows_per_group] or nullptr (accumulated)
+};
+cudaError_t launch_route_select(const SelectArgs& args, cudaStream_t stream);
+
+// ---- (b) sampled block mass ------------------------------------------------
+struct MassArgs {
+  int64_t batch, heads, n_rows;   // rows of the [B, n_rows, H, D] inputs
+  int32_t samples, q_blocks;      // rows (and keys) per block; blocks per row
+  float scale;
+  int32_t round_bf16;
+  const float* block_bias;        // [Qb] additive key weight per key block, or null (0)
+  float mass_scale;               // multiplies each block sum (1/S: mean over query samples)
+  float* mass;                    // [B, H, Qb, Qb]
+  int* err_word;
+};
+cudaError_t launch_sampled_mass(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                const MassArgs& args, cudaStream_t stream);
+
+// ---- (a) block-sparse attention --------------------------------------------
+struct AttnArgs {
+  int64_t batch, tokens, heads;
+  int32_t q_blocks, k_blocks;     // ceil(T / block)
+  int32_t block;                  // 64 or 128
+  int32_t route_cols;             // row stride of indices (>= k_blocks)
+  int64_t route_batch_stride;     // in rows of [H * Qb]; 0 = one route for all batches
+  const int32_t* counts;          // [RB, H, Qb]
+  const int32_t* indices;         // [RB, H, Qb, route_cols]
+  float scale;
+  __nv_bfloat16* out;             // [B, T, H, D] with strides below (elements)
+  int64_t out_stride_b, out_stride_t, out_stride_h;
+  float* lse;                     // [B, H, T] or nullptr
+  int* err_word;
+};
+cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                             const CUtensorMap& tm_v, const AttnArgs& args,
+                             cudaStream_t stream);
+
+}  // namespace bsa

@@ -1,0 +1,109 @@
+// (c) Spatial reorder: out[t][b][i][:] = src[t][b][perm[i]][:] for up to three
+// tensors sharing one permutation.  Pack (Q/K/V into Morton order) and unpack
+// (output back to raster order, with the inverse permutation) are both this
+// gather, so every store is a coalesced full row.
+//
+// Reference semantics: attention_backends/spatial.py:82-93 (index_select on
+// axis 1) and the fused Triton gather attention_backends/layout_ops.py:21-52,
+// 86-125.
+#include "bsa_kernels.h"
+
+namespace bsa {
+namespace {
+
+constexpr int kReorderWarps = 8;
+constexpr int kUnroll = 4;
+
+struct ReorderArgs {
+  const uint8_t* src[3];
+  uint8_t* dst[3];
+  const int32_t* perm;
+  int64_t batch;
+  int64_t tokens_out;
+  int64_t tokens_in;
+  int64_t row_bytes;
+  int64_t rows_per_tensor;  // batch * tokens_out
+  int n_tensors;
+  int* err_word;
+};
+
+// One warp copies one output row per iteration; each lane moves kUnroll
+// vectors per step so several loads are in flight before the stores.
+template <typename Vec>
+__global__ void __launch_bounds__(kReorderWarps * 32)
+    reorder_rows_kernel(const __grid_constant__ ReorderArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (static_cast<int64_t>(blockIdx.x) * kReorderWarps) + (threadIdx.x >> 5);
+  const int64_t total = a.rows_per_tensor * a.n_tensors;
+  const int64_t nvec = a.row_bytes / static_cast<int64_t>(sizeof(Vec));
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kReorderWarps;
+  for (int64_t r = warp_global; r < total; r += warp_stride) {
+    const int t = static_cast<int>(r / a.rows_per_tensor);
+    const int64_t rr = r - static_cast<int64_t>(t) * a.rows_per_tensor;
+    const int64_t b = rr / a.tokens_out;
+    const int64_t i = rr - b * a.tokens_out;
+    int64_t s = __ldg(a.perm + i);
+    if (s < 0 || s >= a.tokens_in) {
+      if (lane == 0 && a.err_word) atomicOr(a.err_word, kErrBadRoute);
+      continue;
+    }
+    const uint8_t* src_base = t == 0 ? a.src[0] : (t == 1 ? a.src[1] : a.src[2]);
+    uint8_t* dst_base = t == 0 ? a.dst[0] : (t == 1 ? a.dst[1] : a.dst[2]);
+    const Vec* src = reinterpret_cast<const Vec*>(src_base + (b * a.tokens_in + s) * a.row_bytes);
+    Vec* dst = reinterpret_cast<Vec*>(dst_base + (b * a.tokens_out + i) * a.row_bytes);
+    int64_t v = lane;
+    for (; v + 32 * (kUnroll - 1) < nvec; v += 32 * kUnroll) {
+      Vec tmp[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) tmp[u] = __ldcs(src + v + 32 * u);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) dst[v + 32 * u] = tmp[u];
+    }
+    for (; v < nvec; v += 32) dst[v] = __ldcs(src + v);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_reorder_rows(int n_tensors, const void* const* src, void* const* dst,
+                                const int32_t* perm, int64_t batch, int64_t tokens_out,
+                                int64_t tokens_in, int64_t row_bytes, int* err_word,
+                                cudaStream_t stream, int num_sms) {
+  ReorderArgs a{};
+  uintptr_t align_bits = static_cast<uintptr_t>(row_bytes);
+  for (int t = 0; t < n_tensors; ++t) {
+    a.src[t] = static_cast<const uint8_t*>(src[t]);
+    a.dst[t] = static_cast<uint8_t*>(dst[t]);
+    align_bits |= reinterpret_cast<uintptr_t>(src[t]) | reinterpret_cast<uintptr_t>(dst[t]);
+  }
+  a.perm = perm;
+  a.batch = batch;
+  a.tokens_out = tokens_out;
+  a.tokens_in = tokens_in;
+  a.row_bytes = row_bytes;
+  a.rows_per_tensor = batch * tokens_out;
+  a.n_tensors = n_tensors;
+  a.err_word = err_word;
+  const int64_t rows = a.rows_per_tensor * n_tensors;
+  if (rows == 0) return cudaSuccess;
+  // Enough warps to keep every SM's load queue full; each warp loops.
+  int64_t blocks = (rows + kReorderWarps - 1) / kReorderWarps;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 16;
+  if (blocks > cap) blocks = cap;
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const dim3 block(kReorderWarps * 32);
+  if ((align_bits & 15) == 0) {
+    reorder_rows_kernel<uint4><<<grid, block, 0, stream>>>(a);
+  } else if ((align_bits & 7) == 0) {
+    reorder_rows_kernel<uint2><<<grid, block, 0, stream>>>(a);
+  } else if ((align_bits & 3) == 0) {
+    reorder_rows_kernel<uint32_t><<<grid, block, 0, stream>>>(a);
+  } else if ((align_bits & 1) == 0) {
+    reorder_rows_kernel<uint16_t><<<grid, block, 0, stream>>>(a);
+  } else {
+    reorder_rows_kernel<uint8_t><<<grid, block, 0, stream>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace bsa

@@ -1,0 +1,268 @@
+"""torch-facing wrappers of the C ABI (one function per entry point of include/bsa.h).
+
+Each wrapper checks shapes/dtypes, allocates the outputs with torch on the
+inputs' device, and enqueues the kernel on the current CUDA stream.  Inputs
+must be CUDA tensors; nothing here has a CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+import math
+from typing import NamedTuple, Sequence
+
+import torch
+
+from . import _native
+
+HEAD_DIM = 128
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "the routed block-sparse path runs only on CUDA tensors "
+                f"(got a {t.device} tensor); it has no CPU implementation")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError("all tensors must be on the same device")
+    return device
+
+
+def _stream(device) -> int:
+    return _native.stream_handle(device)
+
+
+# ----------------------------------------------------------------------------
+# (c) reorder
+# ----------------------------------------------------------------------------
+
+def reorder_rows(tensors: Sequence[torch.Tensor], perm: torch.Tensor,
+                 tokens_out: int | None = None) -> tuple:
+    """Gather token rows: ``out[b, i] = x[b, perm[i]]`` for 1-3 tensors ``[B, T, ...]``.
+
+    Same result as ``x.index_select(1, perm)`` (reference ``spatial.py:82-93``).
+    """
+    tensors = [t.contiguous() for t in tensors]
+    if not 1 <= len(tensors) <= 3:
+        raise ValueError("reorder_rows takes one to three tensors")
+    first = tensors[0]
+    device = _require_cuda(*tensors, perm)
+    if any(t.shape != first.shape or t.dtype != first.dtype for t in tensors):
+        raise ValueError("tensors must share shape and dtype")
+    if first.dim() < 2:
+        raise ValueError("tensors must have a batch and a token axis")
+    perm = perm.to(device=device, dtype=torch.int32).contiguous()
+    if perm.dim() != 1:
+        raise ValueError("perm must be one-dimensional")
+    tokens_out = perm.numel() if tokens_out is None else tokens_out
+    batch, tokens_in = first.shape[0], first.shape[1]
+    row_bytes = first[0, 0].numel() * first.element_size() if tokens_in else 0
+    outs = [torch.empty((batch, tokens_out) + tuple(first.shape[2:]), dtype=first.dtype,
+                        device=device) for _ in tensors]
+    if batch == 0 or tokens_out == 0 or row_bytes == 0:
+        return tuple(outs)
+    n = len(tensors)
+    src = (ctypes.c_void_p * 3)(*([t.data_ptr() for t in tensors] + [0] * (3 - n)))
+    dst = (ctypes.c_void_p * 3)(*([t.data_ptr() for t in outs] + [0] * (3 - n)))
+    _native.call("bsa_reorder_rows", n, src, dst, perm.data_ptr(), batch, tokens_out,
+                 tokens_in, row_bytes, _native.err_word(device).data_ptr(), _stream(device))
+    return tuple(outs)
+
+
+# ----------------------------------------------------------------------------
+# (b) route: sampling, mass, selection, CSR
+# ----------------------------------------------------------------------------
+
+@functools.lru_cache(maxsize=64)
+def _sample_tables(tokens: int, block: int, samples: int):
+    """Sample token ids and per-block key weights (reference ``flex.py:222-237``)."""
+    blocks = math.ceil(tokens / block)
+    block_ids = torch.arange(blocks)
+    sizes = (tokens - block_ids * block).clamp(max=block)
+    sample_ids = torch.arange(samples)
+    local = torch.div((2 * sample_ids + 1)[None] * sizes[:, None], 2 * samples,
+                      rounding_mode="floor").clamp_max(sizes[:, None] - 1)
+    ids = (block_ids[:, None] * block + local).reshape(-1).to(torch.int32)
+    bias = (sizes.float() / samples).log()
+    return ids, bias
+
+
+@functools.lru_cache(maxsize=64)
+def _device_sample_tables(tokens: int, block: int, samples: int, device: torch.device):
+    ids, bias = _sample_tables(tokens, block, samples)
+    return ids.to(device), bias.to(device)
+
+
+def sampled_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128, samples: int = 2,
+                       scale: float | None = None, round_bf16: bool = True) -> torch.Tensor:
+    """Sampled block mass ``[B, H, Qb, Qb]`` fp32 from bf16 ``q, k [B, T, H, D]``.
+
+    Reference ``flex.py:205-251`` (per batch element).
+    """
+    device = _require_cuda(q, k)
+    if q.shape != k.shape or q.dim() != 4:
+        raise ValueError("q and k must be [B, T, H, D] with equal shapes")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise ValueError("sampled_block_mass expects bf16 inputs")
+    if not 0 < samples <= block:
+        raise ValueError("route_samples must be in [1, block_size]")
+    if samples not in (1, 2, 4, 8, 16, 32):
+        raise NotImplementedError("route_samples must be a power of two <= 32 on this path")
+    B, T, H, D = q.shape
+    if D != HEAD_DIM:
+        raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
+    blocks = math.ceil(T / block)
+    ids, bias = _device_sample_tables(T, block, samples, device)
+    sq, sk = reorder_rows([q, k], ids)
+    mass = torch.empty((B, H, blocks, blocks), dtype=torch.float32, device=device)
+    s = float(scale) if scale is not None else D ** -0.5
+    _native.call("bsa_sampled_mass", sq.data_ptr(), sk.data_ptr(), B, H, blocks, samples, D,
+                 bias.data_ptr(), s, 1 if round_bf16 else 0, mass.data_ptr(),
+                 _native.err_word(device).data_ptr(), _stream(device))
+    return mass
+
+
+def exact_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128,
+                     scale: float | None = None) -> torch.Tensor:
+    """Exact dense block mass ``[B, H, Qb, Qb]`` (reference ``flex.py:97-108,167-202``)."""
+    device = _require_cuda(q, k)
+    if q.shape != k.shape or q.dim() != 4:
+        raise ValueError("q and k must be [B, T, H, D] with equal shapes")
+    q = q.to(torch.bfloat16).contiguous()
+    k = k.to(torch.bfloat16).contiguous()
+    B, T, H, D = q.shape
+    if D != HEAD_DIM:
+        raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
+    blocks = math.ceil(T / block)
+    mass = torch.empty((B, H, blocks, blocks), dtype=torch.float32, device=device)
+    s = float(scale) if scale is not None else D ** -0.5
+    _native.call("bsa_exact_block_mass", q.data_ptr(), k.data_ptr(), B, T, H, D, block, s,
+                 mass.data_ptr(), _native.err_word(device).data_ptr(), _stream(device))
+    return mass
+
+
+class RouteCSR(NamedTuple):
+    route: torch.Tensor | None    # uint8 [..., Qb, Kb]
+    counts: torch.Tensor | None   # int32 [..., Qb]
+    indices: torch.Tensor | None  # int32 [..., Qb, Kb]
+    kept: torch.Tensor | None     # int64 [prod(...)] selected blocks per leading index
+
+
+def keep_cap(cols: int, keep: float) -> int:
+    """``max(1, math.ceil(cols * keep))`` exactly as the reference (``flex.py:89``)."""
+    return max(1, math.ceil(cols * keep))
+
+
+def route_select(mass: torch.Tensor, prev: torch.Tensor | None = None, persistence: float = 0.0,
+                 target: float = 0.9, keep: float = 0.625, sink_blocks: int = 0,
+                 want_route: bool = True, want_csr: bool = True,
+                 want_kept: bool = True) -> RouteCSR:
+    """Prior + top-mass + sink + CSR from fp32 ``mass [..., Qb, Kb]``.
+
+    Bit-identical to the reference's ``_top_mass_route`` (``flex.py:83-94``)
+    with the prior of ``flex.py:535-541`` and the sink of ``flex.py:550-566``.
+    """
+    device = _require_cuda(mass, prev)
+    if mass.dtype != torch.float32:
+        raise ValueError("mass must be float32")
+    if not 0 < keep <= 1:
+        raise ValueError("keep must be in (0, 1]")
+    if not 0 < target <= 1:
+        raise ValueError("mass_target must be in (0, 1]")
+    mass = mass.contiguous()
+    cols = mass.shape[-1]
+    rows = mass.numel() // cols if cols else 0
+    group = mass.shape[-2] if mass.dim() >= 2 else 1
+    prev_u8 = None
+    if prev is not None and persistence:
+        if prev.shape != mass.shape:
+            raise ValueError("previous route and mass must have identical shapes")
+        prev_u8 = prev.to(torch.uint8).contiguous()
+    lead = mass.shape[:-1]
+    route = torch.empty(mass.shape, dtype=torch.uint8, device=device) if want_route else None
+    counts = torch.empty(lead, dtype=torch.int32, device=device) if want_csr else None
+    indices = torch.empty(mass.shape, dtype=torch.int32, device=device) if want_csr else None
+    kept = (torch.empty(max(1, rows // max(1, group)), dtype=torch.int64, device=device)
+            if want_kept else None)
+    if rows:
+        _native.call("bsa_route_select", mass.data_ptr(), _native.ptr(prev_u8), rows, cols,
+                     group, float(persistence), float(target), keep_cap(cols, keep),
+                     int(sink_blocks), _native.ptr(route), _native.ptr(counts),
+                     _native.ptr(indices), _native.ptr(kept), _stream(device))
+    return RouteCSR(route, counts, indices, kept)
+
+
+def pack_boolean_rows(route: torch.Tensor):
+    """CSR of a boolean route: counts and ids (selected ascending, then the rest)."""
+    device = _require_cuda(route)
+    if route.dim() < 2:
+        raise ValueError("route must be a boolean tensor with at least two axes")
+    cols = route.shape[-1]
+    r = route.to(torch.uint8).contiguous()
+    counts = torch.empty(route.shape[:-1], dtype=torch.int32, device=device)
+    indices = torch.empty(route.shape, dtype=torch.int32, device=device)
+    rows = r.numel() // cols if cols else 0
+    if rows:
+        _native.call("bsa_pack_boolean_rows", r.data_ptr(), rows, cols, counts.data_ptr(),
+                     indices.data_ptr(), _stream(device))
+    return counts, indices
+
+
+# ----------------------------------------------------------------------------
+# (a) attention
+# ----------------------------------------------------------------------------
+
+def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           counts: torch.Tensor, indices: torch.Tensor, block: int = 128,
+                           scale: float | None = None, out: torch.Tensor | None = None,
+                           return_lse: bool = False):
+    """Block-sparse attention over a CSR route.
+
+    ``q, k, v``: bf16 ``[B, T, H, D]``.  ``counts``: int32 ``[H, Qb]`` (one route
+    for every batch element) or ``[B, H, Qb]``; ``indices``: int32 with a trailing
+    ``route_cols >= Qb`` axis.  Returns bf16 ``[B, T, H, D]`` (and fp32 LSE
+    ``[B, H, T]`` when ``return_lse``).  Reference ``flex.py:358-399``.
+    """
+    device = _require_cuda(q, k, v, counts, indices)
+    if not (q.shape == k.shape == v.shape) or q.dim() != 4:
+        raise ValueError("q, k and v must be [B, T, H, D] with equal shapes")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("block_sparse_attention expects bf16 q, k, v")
+    B, T, H, D = q.shape
+    if D != HEAD_DIM:
+        raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
+    if block not in (64, 128):
+        raise NotImplementedError("block must be 64 or 128")
+    blocks = math.ceil(T / block)
+    if counts.dim() == 2:
+        has_batch = 0
+        expect = (H, blocks)
+    else:
+        has_batch = 1
+        expect = (B, H, blocks)
+    if tuple(counts.shape) != expect:
+        raise ValueError(f"counts shape {tuple(counts.shape)} != {expect}")
+    if tuple(indices.shape[:-1]) != expect or indices.shape[-1] < blocks:
+        raise ValueError("indices must be [..., Qb, route_cols >= Qb] matching counts")
+    if counts.dtype != torch.int32 or indices.dtype != torch.int32:
+        raise ValueError("counts and indices must be int32")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    counts = counts.contiguous()
+    indices = indices.contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=device) if return_lse else None
+    s = float(scale) if scale is not None else D ** -0.5
+    ost = out.stride()
+    _native.call("bsa_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), B, T, H, D,
+                 q.stride(0), q.stride(1), q.stride(2), counts.data_ptr(), indices.data_ptr(),
+                 indices.shape[-1], has_batch, block, s, out.data_ptr(), ost[0], ost[1], ost[2],
+                 _native.ptr(lse), _native.err_word(device).data_ptr(), _stream(device))
+    return (out, lse) if return_lse else out

@@ -1,0 +1,151 @@
+/*
+ * bsa.h -- C ABI of the B200 routed block-sparse attention path (libbsa.so).
+ *
+ * Drop-in for the FlexAttention pieces of the reference study's `flex_reuse`
+ * attention backend (yangshuo1230/DiT_Sparse_Atten, attention_backends/).
+ * Every entry point:
+ *   - takes plain device pointers, sizes and element strides (no framework
+ *     types) and a CUDA stream (cudaStream_t passed as void*; NULL = legacy
+ *     default stream);
+ *   - is stream-ordered and asynchronous: it validates arguments, enqueues
+ *     kernels and returns without synchronising;
+ *   - allocates no memory: outputs and workspaces are caller-owned;
+ *   - returns BSA_OK or a negative status; the message for the last failure on
+ *     the calling thread is available from bsa_last_error().
+ * Kernels that can detect bad data at run time (out-of-range route entries,
+ * a bounded wait that timed out) OR a bit from BSA_DEVICE_* into the
+ * caller-provided int32 `err_word` (device memory) instead of faulting.
+ * Target: sm_100a (NVIDIA B200).
+ */
+#ifndef BSA_H_
+#define BSA_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BSA_API __attribute__((visibility("default")))
+#else
+#define BSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSA_OK 0
+#define BSA_ERR_INVALID_ARGUMENT (-1)
+#define BSA_ERR_UNSUPPORTED (-2)
+#define BSA_ERR_CUDA (-3)
+#define BSA_ERR_NO_DEVICE (-4)
+
+/* Bits a kernel ORs into err_word. */
+#define BSA_DEVICE_WAIT_TIMEOUT 1 /* a bounded mbarrier wait gave up */
+#define BSA_DEVICE_BAD_ROUTE 2    /* a CSR count / block id / permutation entry was out of range */
+#define BSA_DEVICE_TMEM_ALLOC 4   /* tensor-memory allocation returned an unusable address */
+
+/* Library version, major*10000 + minor*100 + patch. */
+BSA_API int bsa_version(void);
+
+/* Message describing the last failed call on this thread ("" if none). */
+BSA_API const char* bsa_last_error(void);
+
+/*
+ * (c) Spatial reorder (gather of whole token rows).
+ * For t < n_tensors (1..3), b < batch, i < tokens_out:
+ *   dst[t][b, i, :] = src[t][b, perm[i], :]
+ * where a token row is `row_bytes` contiguous bytes and rows are contiguous
+ * per batch element ([batch, tokens, row_bytes]).  perm values must lie in
+ * [0, tokens_in); out-of-range entries are skipped and flag BSA_DEVICE_BAD_ROUTE.
+ * Pack is perm = layout permutation, unpack is perm = its inverse.
+ * Replaces: attention_backends/layout_ops.py:86-125 (reorder_qkv) and
+ *           attention_backends/spatial.py:82-93 (reorder / reorder_qkv / restore).
+ */
+BSA_API int bsa_reorder_rows(int32_t n_tensors, const void* const* src, void* const* dst,
+                     const int32_t* perm, int64_t batch, int64_t tokens_out, int64_t tokens_in,
+                     int64_t row_bytes, int32_t* err_word, void* stream);
+
+/*
+ * CSR pack of a boolean route [rows, cols] (uint8 0/1): counts[r] = number of
+ * selected columns; indices[r, :] = selected column ids ascending, then the
+ * unselected ids ascending.  cols <= 4096.
+ * Replaces: attention_backends/layout_ops.py:128-151 (pack_boolean_rows),
+ *           attention_backends/flex.py:275-281 (_pack_route).
+ */
+BSA_API int bsa_pack_boolean_rows(const uint8_t* route, int64_t rows, int32_t cols, int32_t* counts,
+                          int32_t* indices, void* stream);
+
+/*
+ * (b) Route selection from fp32 block mass [rows, cols] (cols <= 4096):
+ *   1. if prev != NULL and persistence != 0:
+ *        mass = mass + persistence * mean_row(mass) * prev          (flex.py:535-541)
+ *   2. top-mass: sort the row descending (ties: lower block id first), keep the
+ *      first min(#(cumsum < sum * target) + 1, max_blocks), where the caller
+ *      computes max_blocks = max(1, ceil(cols * keep)) as the reference does
+ *      (in double precision)                                       (flex.py:83-94)
+ *   3. force columns [0, sink_blocks) on                           (flex.py:550-566)
+ *   4. write route_out [rows, cols] uint8, counts [rows], indices [rows, cols]
+ *      (CSR as bsa_pack_boolean_rows) and, per group of rows_per_group
+ *      consecutive rows, kept[g] = number of selected blocks     (flex.py:473-493)
+ * The float32 sums follow the reference's PyTorch CPU evaluation order, so the
+ * route is bit-identical to the reference's from the same mass.  Any of
+ * route_out / counts / indices / kept may be NULL.  kept is overwritten.
+ */
+BSA_API int bsa_route_select(const float* mass, const uint8_t* prev, int64_t rows, int32_t cols,
+                     int32_t rows_per_group, float persistence, float target,
+                     int32_t max_blocks, int32_t sink_blocks, uint8_t* route_out,
+                     int32_t* counts, int32_t* indices, uint64_t* kept, void* stream);
+
+/*
+ * (b) Sampled block mass.  sampled_q / sampled_k: bf16 [batch, q_blocks * samples,
+ * heads, head_dim] contiguous (rows gathered with bsa_reorder_rows through the
+ * sample token ids of flex.py:222-231).  block_bias: fp32 [q_blocks], the
+ * per-key-block log(block_size_b / samples) of flex.py:236-237.  Writes
+ * mass: fp32 [batch, heads, q_blocks, q_blocks].  samples in {1,2,4,8,16,32},
+ * head_dim == 128, q_blocks <= 4096.  round_bf16 != 0 reproduces the bf16
+ * score rounding of the reference (flex.py:245).
+ * Replaces: attention_backends/flex.py:205-251 (_sampled_block_mass).
+ */
+BSA_API int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch, int64_t heads,
+                     int32_t q_blocks, int32_t samples, int32_t head_dim,
+                     const float* block_bias, float scale, int32_t round_bf16, float* mass,
+                     int32_t* err_word, void* stream);
+
+/*
+ * (b) Exact dense block mass (the exact bootstrap / refresh route source):
+ *   mass[b, h, qb, kb] = sum_{q in qb, k in kb, q,k < tokens} softmax_q(k)
+ * over full-precision scores (no bf16 rounding) of q, k: bf16 [batch, tokens,
+ * heads, head_dim] contiguous.  Writes fp32 [batch, heads, Qb, Qb].
+ * block in {32, 64, 128}, head_dim == 128, Qb <= 4096.
+ * Replaces: attention_backends/flex.py:97-108,167-202 (_block_attention_mass,
+ *           given the LSE of the dense FlexAttention pass of flex.py:254-272).
+ */
+BSA_API int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t tokens,
+                         int64_t heads, int32_t head_dim, int32_t block, float scale, float* mass,
+                         int32_t* err_word, void* stream);
+
+/*
+ * (a) Block-sparse attention forward.
+ * q, k, v: bf16 [batch, tokens, heads, head_dim] with element strides
+ * (in_stride_b, in_stride_t, in_stride_h) shared by q, k and v; the head_dim
+ * stride is 1.  out: bf16 with its own strides.  Route: counts [RB, heads, Qb]
+ * and indices [RB, heads, Qb, route_cols] int32 (CSR, first counts[] entries
+ * used), Qb = ceil(tokens / block); RB = batch if route_has_batch else 1.
+ * Query block qb of head h attends to all keys < tokens of the listed key
+ * blocks; rows with an empty route produce zeros.  lse (optional, fp32
+ * [batch, heads, tokens]) receives the natural-log row log-sum-exp.
+ * block in {64, 128}; head_dim == 128; strides * 2 bytes multiple of 16.
+ * Replaces: attention_backends/flex.py:358-399 (_flex_output/_flex_kernel over
+ *           the BlockMask of flex.py:308-355).
+ */
+BSA_API int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
+                      int64_t heads, int32_t head_dim, int64_t in_stride_b, int64_t in_stride_t,
+                      int64_t in_stride_h, const int32_t* counts, const int32_t* indices,
+                      int32_t route_cols, int32_t route_has_batch, int32_t block, float scale,
+                      void* out, int64_t out_stride_b, int64_t out_stride_t,
+                      int64_t out_stride_h, float* lse, int32_t* err_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSA_H_ */

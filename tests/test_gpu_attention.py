@@ -1,0 +1,155 @@
+"""GPU parity of the block-sparse attention kernel (a).
+
+Tolerance: bf16 output within max-abs 2e-2 and
+mean-abs 2e-3 of the fp32 reference.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import unpack_route
+from dit_sparse_atten_b200 import _native, kernels, synthetic
+from dit_sparse_atten_b200.spatial import build_spatial_layout, tile_major_layout
+from oracle import attention as oatt
+from oracle import route as oroute
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+def assert_attention_close(actual, expected, max_abs=MAX_ABS, mean_abs=MEAN_ABS):
+    diff = np.abs(np.asarray(actual, np.float64) - np.asarray(expected, np.float64))
+    assert np.isfinite(diff).all()
+    assert diff.max() <= max_abs, diff.max()
+    assert diff.mean() <= mean_abs, diff.mean()
+
+
+def run(q, k, v, route, block, **kw):
+    """Attention through the CSR built on the GPU; route bool [H, Qb, Kb] or [B, H, Qb, Kb]."""
+    counts, indices = kernels.pack_boolean_rows(torch.as_tensor(route, device=DEV))
+    out = kernels.block_sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), counts, indices,
+                                         block=block, **kw)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    return out
+
+
+def test_config1_block64_matches_reference(golden):
+    g = golden("config1.npz")
+    q, k, v, route = synthetic.config1_inputs(seed=0)
+    lay = tile_major_layout((3, 8, 16), 8, 8)
+    qb, kb, vb = (x.to(torch.bfloat16).to(DEV) for x in (q, k, v))
+    qt, kt, vt = lay.reorder_qkv(qb, kb, vb)
+    out_t = run(qt, kt, vt, route, 64)
+    out = lay.restore(out_t).float().cpu().numpy()
+    assert_attention_close(out, g["output"])
+
+
+@pytest.mark.parametrize("tokens,heads,block,density,seed", [
+    (256, 2, 128, 0.6, 0), (250, 2, 128, 0.5, 1), (1000, 3, 128, 0.3, 2),
+    (777, 2, 64, 0.5, 3), (384, 4, 64, 0.8, 4), (4096, 2, 128, 0.625, 5)])
+def test_random_routes_match_oracle(tokens, heads, block, density, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn((1, tokens, heads, 128), generator=g).to(torch.bfloat16)
+               for _ in range(3))
+    blocks = math.ceil(tokens / block)
+    route = torch.rand((heads, blocks, blocks), generator=g) < density
+    route |= torch.eye(blocks, dtype=torch.bool)
+    out = run(q, k, v, route, block)
+    ref = oatt.block_sparse_attention(q[0].float().numpy(), k[0].float().numpy(),
+                                      v[0].float().numpy(), route.numpy(), block)
+    assert_attention_close(out[0].float().cpu().numpy(), ref)
+
+
+def test_reference_explicit_block_mask_case():
+    """tests/test_flex_backend.py:122-148 at head_dim 128: identity route, partial tail."""
+    torch.manual_seed(1)
+    q, k, v = (torch.randn(1, 250, 2, 128).to(torch.bfloat16) for _ in range(3))
+    route = torch.eye(2, dtype=torch.bool).expand(2, -1, -1).contiguous()
+    out = run(q, k, v, route, 128)
+    ref = oatt.dense_masked_attention(q[0].float().numpy(), k[0].float().numpy(),
+                                      v[0].float().numpy(), route.numpy(), 128)
+    assert_attention_close(out[0].float().cpu().numpy(), ref)
+
+
+def test_empty_rows_are_zero_and_lse():
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn((2, 300, 2, 128), generator=g).to(torch.bfloat16) for _ in range(3))
+    route = torch.rand((2, 2, 3, 3), generator=g) < 0.5
+    route[0, 0, 1] = False
+    route[1, 1, 2] = True
+    counts, indices = kernels.pack_boolean_rows(route.to(DEV))
+    out, lse = kernels.block_sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), counts, indices,
+                                              block=128, return_lse=True)
+    torch.cuda.synchronize()
+    for b in range(2):
+        ref, ref_lse = oatt.block_sparse_attention(
+            q[b].float().numpy(), k[b].float().numpy(), v[b].float().numpy(),
+            route[b].numpy(), 128, return_lse=True)
+        got = out[b].float().cpu().numpy()
+        assert_attention_close(got, ref)
+        lse_got = lse[b].cpu().numpy()
+        finite = np.isfinite(ref_lse)
+        np.testing.assert_allclose(lse_got[finite], ref_lse[finite], atol=2e-2, rtol=1e-3)
+        assert np.isneginf(lse_got[~finite]).all()
+    assert (out[0, 128:256, 0] == 0).all()
+
+
+def test_shared_route_across_batch():
+    g = torch.Generator().manual_seed(8)
+    q, k, v = (torch.randn((2, 512, 2, 128), generator=g).to(torch.bfloat16) for _ in range(3))
+    route = torch.rand((2, 4, 4), generator=g) < 0.6
+    route |= torch.eye(4, dtype=torch.bool)
+    out = run(q, k, v, route, 128)
+    for b in range(2):
+        ref = oatt.block_sparse_attention(q[b].float().numpy(), k[b].float().numpy(),
+                                          v[b].float().numpy(), route.numpy(), 128)
+        assert_attention_close(out[b].float().cpu().numpy(), ref)
+
+
+def test_config2_480p_layer(golden):
+    """Full config 2 (B=2, 32,760 tokens, 12 heads, partial tail) on blob routes."""
+    cfg = synthetic.CONFIG2
+    routes = unpack_route(golden("blob_routes.npz")["c2_route"], cfg.blocks)
+    q, k, v = synthetic.wan_qkv(cfg, seed=21, device=DEV)
+    out = run(q, k, v, torch.from_numpy(routes), 128)
+    assert torch.isfinite(out).all()
+    heads = [0, 5, 11]
+    qbs = [0, 1, 100, cfg.blocks - 2, cfg.blocks - 1]
+    rows = np.concatenate([np.arange(qb * 128, min(cfg.tokens, qb * 128 + 128)) for qb in qbs])
+    for b in range(cfg.batch):
+        qs, ks, vs = (x[b][:, heads].float().cpu().numpy() for x in (q, k, v))
+        ref = oatt.block_sparse_attention(qs, ks, vs, routes[b][heads], 128, query_blocks=qbs,
+                                          dtype=np.float32)
+        got = out[b][:, heads].float().cpu().numpy()
+        assert_attention_close(got[rows], ref[rows])
+
+
+def test_config4_720p_layer_morton(golden):
+    """Config 4 (B=2, 57,600 tokens, 40 heads): pack, attention, unpack; sampled rows."""
+    cfg = synthetic.CONFIG4
+    routes = unpack_route(golden("blob_routes.npz")["c4_route"], cfg.blocks)
+    lay = build_spatial_layout(cfg.grid, 128)
+    q, k, v = synthetic.wan_qkv(cfg, seed=41, device=DEV)
+    qp, kp, vp = lay.reorder_qkv(q, k, v)
+    out_p = run(qp, kp, vp, torch.from_numpy(routes), 128)
+    out = lay.restore(out_p)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out_p).all()
+    heads = [0, 13, 39]
+    qbs = [0, 7, 225, 449]
+    rows = np.concatenate([np.arange(qb * 128, qb * 128 + 128) for qb in qbs])
+    for b in range(cfg.batch):
+        qs, ks, vs = (x[b][:, heads].float().cpu().numpy() for x in (qp, kp, vp))
+        ref = oatt.block_sparse_attention(qs, ks, vs, routes[b][heads], 128, query_blocks=qbs,
+                                          dtype=np.float32)
+        got = out_p[b][:, heads].float().cpu().numpy()
+        assert_attention_close(got[rows], ref[rows])
+    perm = lay.permutation_cpu.long().to(DEV)
+    assert torch.equal(out[:, perm[:512]].view(torch.int16), out_p[:, :512].view(torch.int16))
