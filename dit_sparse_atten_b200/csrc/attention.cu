@@ -101,9 +101,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&bar->slot_full[s], 1);
       mbar_init(&bar->slot_empty[s], 1);
     }
-    bar->abort = 0;
+    bar->abort = prior_timeout(a.err_word) ? 1 : 0;
     fence_mbar_init();
   }
+  __syncthreads();
+  if (bar->abort) return;  // uniform: set before the barrier, read after it
   if (BK == 64 && threadIdx.x < 128) {
     // Rows 64..127 of the Q panels are never loaded; keep them finite.
     uint4 zero = make_uint4(0, 0, 0, 0);

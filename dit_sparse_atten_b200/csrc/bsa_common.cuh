@@ -83,11 +83,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   for (uint32_t poll = 1; poll < kWaitMaxPolls; ++poll) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if ((poll & 63) == 0 && global_timer_ns() - start > kWaitTimeoutNs) break;
+    if ((poll & 63) == 0) {
+      // Another CTA of this launch (or an earlier one) already timed out.
+      if (err_word && (*reinterpret_cast<volatile int*>(err_word) & kErrWaitTimeout)) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (global_timer_ns() - start > kWaitTimeoutNs) break;
+    }
   }
   *abort_flag = 1;
   if (err_word) atomicOr(err_word, kErrWaitTimeout);
   return false;
+}
+
+// True when an earlier timeout was recorded in the error word: kernels then
+// skip their work so a systemic failure ends quickly instead of timing out
+// CTA by CTA.  Cleared by the host when it reads the word.
+__device__ __forceinline__ bool prior_timeout(const int* err_word) {
+  return err_word && (*reinterpret_cast<const volatile int*>(err_word) & kErrWaitTimeout);
 }
 
 // ---------------------------------------------------------------------------

@@ -79,9 +79,11 @@ __global__ void __launch_bounds__(kMassThreads, 1)
       mbar_init(&bar->slot_full[s], 1);
       mbar_init(&bar->slot_empty[s], 1);
     }
-    bar->abort = 0;
+    bar->abort = prior_timeout(a.err_word) ? 1 : 0;
     fence_mbar_init();
   }
+  __syncthreads();
+  if (bar->abort) return;  // uniform: set before the barrier, read after it
   for (int i = threadIdx.x; i < a.q_blocks; i += kMassThreads)
     sBias[i] = a.block_bias != nullptr ? a.block_bias[i] : 0.f;
   if (warp == 5) tmem_alloc(&bar->tmem_base, 256);
