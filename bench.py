@@ -1,0 +1,489 @@
+#!/usr/bin/env python
+"""Benchmark of the routed block-sparse attention layer.
+
+One step = one pass of the hot path over one CFG batch of the Wan2.1-14B 720p
+self-attention layer: Morton pack of Q/K/V (1x16 microtiles), block-sparse
+attention over the per-(branch, head, query-block) CSR routes, unpack of the
+output.  57,600 tokens, CFG batch 2, 40 heads, head_dim 128, bf16, routes from
+the seeded Gaussian-blob procedure (top-mass 0.95, keep cap 0.625, 29 sink
+blocks).  Inputs (3 x 1.18 GB) are larger than L2, so no flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl bsa|reference]
+
+N > 1 runs under torchrun: CFG branches on two rank groups, heads split inside
+a group with a sequence<->head all-to-all (NCCL); value is the whole-job rate
+at fixed total work ("strong").  ``--impl reference`` times the reference's CPU
+algorithm (the oracle port) on rank 0 with all host cores.
+Prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+METRIC = "Wan-14B 57.6k-token sparse attn layer ms & eff. TFLOPS; 5-step forward sec"
+UNIT = "TFLOPS"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch (ncu), or None.
+ATTENTION_TRAFFIC_BYTES = None
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("bsa", "reference"), default="bsa")
+    p.add_argument("--heads", type=int, default=40, help="heads (40 = config 4; fewer for profiling)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-route-stage", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="target CPU time of the cpu_baseline sample")
+    return p.parse_args(argv)
+
+
+def load_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+
+def layer_config(heads):
+    from dit_sparse_atten_b200 import synthetic
+    c = synthetic.CONFIG4
+    return synthetic.LayerConfig(c.name, c.grid, c.batch, heads, c.head_dim, c.block,
+                                 c.mass_target, c.keep)
+
+
+def blob_scores(cfg):
+    """Per-branch blob block scores [B, H, Qb, Kb] (CPU, seeds 100 + branch)."""
+    from dit_sparse_atten_b200 import synthetic
+    full = synthetic.CONFIG4.heads
+    return torch.stack([synthetic.blob_scores(full, cfg.blocks, seed=100 + b)[:cfg.heads]
+                        for b in range(cfg.batch)])
+
+
+def kept_flops(route, tokens, block, dim):
+    """Algorithmic FLOPs of QK^T + PV over kept blocks: sum 4 * q_valid * k_valid * D."""
+    blocks = route.shape[-1]
+    sizes = torch.clamp(tokens - torch.arange(blocks, dtype=torch.float64) * block, max=block)
+    per = (sizes[:, None] * sizes[None, :]).to(route.device)
+    return float(4.0 * dim * (route.to(torch.float64) * per).sum())
+
+
+# ----------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm on the host (oracle port)
+# ----------------------------------------------------------------------------
+
+class CpuSample:
+    """Per-(branch, head) query-block work of the config-4 layer on the host.
+
+    The reference's CPU path (sparse.py:670-751 semantics): gather the kept key
+    blocks of one (head, query block), masked softmax, PV, in float32.
+    """
+
+    def __init__(self, cfg):
+        from oracle import route as oroute
+        scores = blob_scores(cfg).numpy()
+        self.routes = oroute.add_first_frame_sink(
+            oroute.top_mass_route(scores, cfg.mass_target, cfg.keep), cfg.grid, cfg.block)
+        self.cfg = cfg
+        g = torch.Generator().manual_seed(41)
+        shape = (cfg.tokens, 128)
+        self.qkv = [torch.randn(shape, generator=g).to(torch.bfloat16).float().numpy()
+                    for _ in range(3)]
+        self.cursor = 0
+
+    def run(self, qblocks):
+        """Attention for the next ``qblocks`` query blocks; returns kept FLOPs."""
+        from oracle import attention as oatt
+        cfg = self.cfg
+        q, k, v = self.qkv
+        flops = 0.0
+        for _ in range(qblocks):
+            idx = self.cursor % (cfg.batch * cfg.heads * cfg.blocks)
+            self.cursor += 1
+            b, rest = divmod(idx, cfg.heads * cfg.blocks)
+            h, qb = divmod(rest, cfg.blocks)
+            route = self.routes[b, h][None]
+            oatt.block_sparse_attention(q[:, None], k[:, None], v[:, None], route, cfg.block,
+                                        query_blocks=[qb], dtype=np.float32)
+            flops += 4.0 * 128 * 128 * 128 * float(route[0, qb].sum())
+        return flops
+
+
+def cpu_threads():
+    return os.cpu_count() or 1
+
+
+def run_cpu_baseline(cfg, seconds):
+    torch.set_num_threads(cpu_threads())
+    sample = CpuSample(cfg)
+    sample.run(2)  # warm-up
+    flops, t0, blocks = 0.0, time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds or blocks < 8:
+        flops += sample.run(4)
+        blocks += 4
+    dt = time.perf_counter() - t0
+    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": f"{blocks} (branch, head, query-block) rows of config 4 through the numpy "
+                      f"oracle port (float32, {dt:.1f} s)"}
+
+
+def run_reference_arm(args):
+    """``--impl reference``: the reference's CPU algorithm, rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    cfg = layer_config(40)
+    torch.set_num_threads(cpu_threads())
+    sample = CpuSample(cfg)
+    per_step = 6
+    for _ in range(max(1, args.warmup)):
+        sample.run(per_step)
+    flops, t0 = 0.0, time.perf_counter()
+    for _ in range(args.steps):
+        flops += sample.run(per_step)
+    dt = time.perf_counter() - t0
+    value = flops / dt / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic (seeded N(0,1) bf16-valued Q/K/V; blob routes of config 4)",
+        "config": {"workload": "config4_wan14b_720p: 57,600 tokens, CFG batch 2, 40 heads, "
+                               "head_dim 128, keep cap 0.625, sink 29",
+                   "step_sample": f"{per_step} (branch, head, query-block) rows per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{per_step * args.steps} query-block rows of config 4 "
+                                   "(oracle port of the reference sparse path)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch.distributed as dist
+
+    from dit_sparse_atten_b200 import _native, kernels, parallel, synthetic
+    from dit_sparse_atten_b200.spatial import build_spatial_layout
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    _native.load_library()
+
+    cfg = layer_config(args.heads)
+    plan = parallel.make_plan(world, rank, cfg.heads, batch=cfg.batch)
+    group = parallel.new_groups(plan) if world > 1 else None
+    branches = plan.branches(cfg.batch)
+    hs = plan.head_slice
+    P = plan.group_size
+
+    # routes: blob scores -> GPU selection (bit-identical to the reference's rule)
+    scores = blob_scores(cfg)
+    sel = kernels.route_select(scores.to(device), target=cfg.mass_target, keep=cfg.keep,
+                               sink_blocks=cfg.sink_blocks)
+    route_all = sel.route.bool()                                   # [B, H, Qb, Kb]
+    total_flops = kept_flops(route_all, cfg.tokens, cfg.block, cfg.head_dim)
+    keep_fraction = float(route_all.float().mean())
+    local_route = route_all[branches][:, hs].contiguous()
+    counts, indices = kernels.pack_boolean_rows(local_route)
+
+    layout = build_spatial_layout(cfg.grid, cfg.block)
+    q, k, v = synthetic.wan_qkv(cfg, seed=41, device=device)
+    q, k, v = (x[branches].contiguous() for x in (q, k, v))
+    t_local = cfg.tokens // P
+    seq = slice(plan.group_rank * t_local, (plan.group_rank + 1) * t_local)
+    if P > 1:
+        q, k, v = (x[:, seq].contiguous() for x in (q, k, v))
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    attn_events = []
+
+    def attend(qh, kh, vh):
+        qp, kp, vp = layout.reorder_qkv(qh, kh, vh)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        out_p = kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=cfg.block)
+        e1.record(stream)
+        attn_events.append((e0, e1))
+        return layout.restore(out_p)
+
+    def step():
+        if P > 1:
+            return parallel.head_parallel_attention(q, k, v, attend, group, P)
+        return attend(q, k, v)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    attn_events.clear()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_events)
+    _native.check_device_errors()
+    if world > 1:
+        t = torch.tensor([ms, attn_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms = float(t[0]), float(t[1])
+
+    # per-stage breakdown (one extra step, rank-local)
+    stages = {}
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    qh, kh, vh = (q, k, v) if P == 1 else (None, None, None)
+    if P == 1:
+        ev[0].record(stream)
+        qp, kp, vp = layout.reorder_qkv(q, k, v)
+        ev[1].record(stream)
+        out_p = kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=cfg.block)
+        ev[2].record(stream)
+        layout.restore(out_p)
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+        elem = q.numel() * q.element_size()
+        pack_ms, unpack_ms = ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])
+        stages = {"pack_ms": pack_ms, "attention_ms": ev[1].elapsed_time(ev[2]),
+                  "unpack_ms": unpack_ms,
+                  "pack_hbm_gbs": 6 * elem / pack_ms / 1e6,
+                  "unpack_hbm_gbs": 2 * elem / unpack_ms / 1e6}
+        if not args.no_route_stage:
+            stages.update(route_stage(cfg, qp, kp, local_route, kernels, device, stream))
+
+    peaks, peak_src = load_peaks()
+    local_flops = kept_flops(local_route, cfg.tokens, cfg.block, cfg.head_dim)
+    achieved = local_flops / (attn_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops_sustained"],
+                "traffic": ATTENTION_TRAFFIC_BYTES,
+                "peak_source": f"bf16_tflops_sustained ({peak_src})",
+                "frac_of_burst": achieved / peaks["bf16_tflops"],
+                "kernel": "bsa_attention_kernel<128>", "kernel_ms": attn_ms,
+                "flops_per_launch": local_flops}
+
+    value = total_flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded Wan-like RMS-normed + 3D-RoPE Q/K, N(0,1) V; blob routes)",
+        "config": {
+            "workload": "config4_wan14b_720p: one self-attention layer, CFG batch 2",
+            "tokens": cfg.tokens, "heads": cfg.heads, "head_dim": cfg.head_dim,
+            "cfg_batch": cfg.batch, "block": cfg.block, "grid": list(cfg.grid),
+            "microtile": list(layout.microtile_shape), "keep_fraction": keep_fraction,
+            "kept_flops": total_flops,
+            "dense_equivalent_tflops": 4.0 * cfg.tokens ** 2 * cfg.heads * cfg.head_dim
+            * cfg.batch / (ms * 1e-3) / 1e12,
+            "parallelism": ("single GPU" if world == 1 else
+                            f"{plan.cfg_groups} CFG group(s) x {P}-way head parallel "
+                            "(Ulysses all-to-all, NCCL)"),
+            "l2": "inputs (3 x 1.18 GB) exceed L2; no flush"},
+        "stages": stages,
+        "roofline": roofline,
+        "gpu_launches": 3 * args.steps * world,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = run_cpu_baseline(cfg, args.cpu_seconds)
+    if not args.no_e2e:
+        line["e2e"] = run_e2e(args, cfg, plan, group, branches, local_route, layout, device,
+                              total_flops)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def route_stage(cfg, qp, kp, route, kernels, device, stream):
+    """Route decision on this layer: sampled mass (S=16) + prior + top-mass + sink + CSR."""
+    prev = route
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(2):
+        mass = kernels.sampled_block_mass(qp, kp, cfg.block, 16)
+        kernels.route_select(mass, prev, 0.5, cfg.mass_target, cfg.keep, cfg.sink_blocks)
+    ev[0].record(stream)
+    mass = kernels.sampled_block_mass(qp, kp, cfg.block, 16)
+    ev[1].record(stream)
+    kernels.route_select(mass, prev, 0.5, cfg.mass_target, cfg.keep, cfg.sink_blocks)
+    ev[2].record(stream)
+    torch.cuda.synchronize()
+    mass_ms, select_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    B, H, Qb = mass.shape[0], mass.shape[1], mass.shape[2]
+    sampled = 2 * B * H * Qb * 16 * cfg.head_dim * 2
+    select_bytes = B * H * Qb * Qb * (4 + 1 + 1 + 4) + B * H * Qb * 4
+    return {"route_mass_ms": mass_ms, "route_select_ms": select_ms,
+            "route_mass_tflops": 2 * 2 * B * H * (Qb * 16) ** 2 * cfg.head_dim / mass_ms / 1e9,
+            "route_select_hbm_gbs": select_bytes / select_ms / 1e6,
+            "route_mass_hbm_gbs": (sampled + B * H * Qb * Qb * 4) / mass_ms / 1e6}
+
+
+def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total_flops):
+    """Same step through the public backend API, pinned host buffers in and out."""
+    import torch.distributed as dist
+
+    from dit_sparse_atten_b200 import parallel, synthetic
+    from dit_sparse_atten_b200.context import set_routing_context
+    from dit_sparse_atten_b200.flex import FlexReuseBackend, FlexReuseConfig
+
+    world = plan.world
+    P = plan.group_size
+    backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True, bootstrap_mode="sampled",
+                                               keep=cfg.keep, mass_target=cfg.mass_target))
+    heads_local = plan.heads_per_rank
+    for i, b in enumerate(branches):
+        backend.install_route(local_route[i], attention_id=1, branch=b, tokens=cfg.tokens,
+                              heads=heads_local, head_dim=cfg.head_dim, device=device,
+                              grid=cfg.grid)
+    t_local = cfg.tokens // P
+    g = torch.Generator().manual_seed(77)
+    host = [torch.randn((len(branches), t_local, cfg.heads, cfg.head_dim), generator=g)
+            .to(torch.bfloat16).pin_memory() for _ in range(3)]
+    out_host = torch.empty_like(host[0]).pin_memory()
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        dq, dk, dv = (h.to(device, non_blocking=True) for h in host)
+        outs = []
+        for i, b in enumerate(branches):
+            set_routing_context(attention_id=1, step=1, branch=b, grid=cfg.grid)
+
+            def attend(qh, kh, vh, _b=b):
+                return backend(qh, kh, vh)
+
+            qi, ki, vi = dq[i:i + 1], dk[i:i + 1], dv[i:i + 1]
+            if P > 1:
+                outs.append(parallel.head_parallel_attention(qi, ki, vi, attend, group, P))
+            else:
+                outs.append(attend(qi, ki, vi))
+        out = torch.cat(outs, 0)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    per_rank_in = sum(h.numel() * h.element_size() for h in host)
+    return {"value": total_flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "h2d_bytes_per_step": per_rank_in * world,
+            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() * world,
+            "api": "FlexReuseBackend.__call__ (reuse phase, spatial reorder) per CFG branch"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

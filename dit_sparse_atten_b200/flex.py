@@ -372,6 +372,30 @@ class FlexReuseBackend:
         }
         self.phase_counts[phase] += 1
 
+    def install_route(self, route, *, attention_id, branch, tokens, heads, head_dim, device,
+                      grid=None, step=0):
+        """Seed the reusable route of one layer and CFG branch.
+
+        ``route``: bool ``[H, Qb, Kb]`` over route blocks in the backend's
+        token order (Morton-packed when ``spatial_reorder`` is on).  The next
+        call with this layer/branch at a later step reuses it exactly as a
+        route produced by a bootstrap would be reused.  Returns the state.
+        """
+        layout = self._spatial_layout(grid, tokens)
+        if self.config.spatial_reorder and layout is None:
+            raise ValueError("spatial_reorder needs a grid whose product is the token count")
+        route = route.to(device=device, dtype=torch.bool)
+        key = (attention_id, branch, tokens, heads, head_dim, route.device,
+               layout.signature if layout is not None else None)
+        state = {"route": route, "frontier": None, "step": step, "layout": layout, "grid": grid,
+                 "kept": route.reshape(route.shape[0], -1).sum(-1),
+                 "block_mask": _build_block_mask(route, tokens, self.config.block_size)}
+        if layout is not None:
+            state["frontier"] = frontier_mask(route, layout.neighbors(route.device))
+        self._update_dispatch(state)
+        self.state[key] = state
+        return state
+
     def profile_summary(self):
         active = [s for s in self.state.values() if s.get("route") is not None]
         keep = [s.get("keep") for s in active] + [

@@ -1,0 +1,120 @@
+"""Head-parallel (Ulysses) execution of the routed attention across GPUs.
+
+The reference runs on one device.  Routes, masses, CSR and attention are all
+per head, so the path partitions by heads: a sequence-parallel caller holding
+``[B, T/P, H, D]`` shards exchanges them with one all-to-all into head shards
+``[B, T, H/P, D]``, runs the local pack -> attention -> unpack, and exchanges
+the output back.  The only cross-head coupling of the reference is the
+dense-dispatch keep fraction (``flex.py:473-493``), a mean over all heads,
+which needs one integer all-reduce (``FlexReuseBackend(process_group=...)``).
+
+With an even number of ranks the two CFG branches (the reference's two
+batch-1 calls per denoising step) run on separate rank groups, which halves
+the all-to-all group.  Collectives go through ``torch.distributed`` (NCCL on
+GPUs, gloo on CPU for tests).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class ParallelPlan:
+    """Placement of one attention layer's (branch, head) work on the ranks."""
+    world: int
+    rank: int
+    cfg_groups: int           # 1 or 2 rank groups (one CFG branch each)
+    group_size: int           # ranks sharing one branch (all-to-all width)
+    group_index: int          # which branch group this rank belongs to
+    group_rank: int           # rank within the group
+    heads: int
+
+    @property
+    def heads_per_rank(self):
+        return self.heads // self.group_size
+
+    @property
+    def head_slice(self):
+        start = self.group_rank * self.heads_per_rank
+        return slice(start, start + self.heads_per_rank)
+
+    def branches(self, batch):
+        """CFG branches (batch indices) this rank's group processes."""
+        if self.cfg_groups == 1:
+            return list(range(batch))
+        per = math.ceil(batch / self.cfg_groups)
+        return list(range(self.group_index * per, min(batch, (self.group_index + 1) * per)))
+
+
+def make_plan(world, rank, heads, batch=2, split_cfg=True):
+    cfg_groups = 2 if (split_cfg and batch >= 2 and world >= 2 and world % 2 == 0) else 1
+    group_size = world // cfg_groups
+    if heads % group_size:
+        raise ValueError(f"{heads} heads do not split over {group_size} ranks")
+    return ParallelPlan(world, rank, cfg_groups, group_size, rank // group_size,
+                        rank % group_size, heads)
+
+
+def new_groups(plan):
+    """Create the CFG rank groups (every rank calls this with the same plan)."""
+    if plan.cfg_groups == 1:
+        return dist.group.WORLD
+    mine = None
+    for g in range(plan.cfg_groups):
+        ranks = list(range(g * plan.group_size, (g + 1) * plan.group_size))
+        pg = dist.new_group(ranks)
+        if g == plan.group_index:
+            mine = pg
+    return mine
+
+
+def seq_to_head(x, group, group_size):
+    """``[B, T/P, H, D]`` sequence shard -> ``[B, T, H/P, D]`` head shard."""
+    if group_size == 1:
+        return x.contiguous()
+    b, t_local, h, d = x.shape
+    hp = h // group_size
+    send = x.reshape(b, t_local, group_size, hp, d).permute(2, 0, 1, 3, 4).contiguous()
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    # recv[src] holds tokens [src*T/P, (src+1)*T/P) of this rank's heads
+    return recv.permute(1, 0, 2, 3, 4).reshape(b, group_size * t_local, hp, d)
+
+
+def head_to_seq(x, group, group_size):
+    """``[B, T, H/P, D]`` head shard -> ``[B, T/P, H, D]`` sequence shard."""
+    if group_size == 1:
+        return x.contiguous()
+    b, t, hp, d = x.shape
+    t_local = t // group_size
+    send = x.reshape(b, group_size, t_local, hp, d).permute(1, 0, 2, 3, 4).contiguous()
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    # recv[src] holds this rank's tokens for the heads of rank src
+    return recv.permute(1, 2, 0, 3, 4).reshape(b, t_local, group_size * hp, d)
+
+
+def head_parallel_attention(q, k, v, attend, group, group_size):
+    """Run ``attend(q, k, v) -> out`` on head shards of sequence-sharded inputs.
+
+    ``q, k, v``: ``[B, T/P, H, D]``; ``attend`` receives ``[B, T, H/P, D]``
+    tensors and returns the same shape (for example pack -> block-sparse
+    attention over this rank's heads' CSR routes -> unpack).
+    """
+    stacked = torch.cat([q, k, v], 0)             # one exchange for Q, K and V
+    heads = seq_to_head(stacked, group, group_size)
+    b = q.shape[0]
+    out = attend(heads[:b], heads[b:2 * b], heads[2 * b:])
+    return head_to_seq(out, group, group_size)
+
+
+def all_reduce_count(count, group=None):
+    """Sum an integer count over the group (the dense-dispatch keep numerator)."""
+    t = count.clone() if torch.is_tensor(count) else torch.tensor([int(count)])
+    dist.all_reduce(t, group=group)
+    return t

@@ -143,8 +143,9 @@ def test_select_blob_routes_bit_exact(golden, name, cfg):
     g = golden("blob_routes.npz")
     routes = unpack_route(g[f"{name}_route"], cfg.blocks)
     for branch in range(cfg.batch):
-        scores = synthetic.blob_scores(cfg.heads, cfg.blocks, seed=100 + branch, device=DEV)
-        r = kernels.route_select(scores, target=cfg.mass_target, keep=cfg.keep,
+        scores = synthetic.blob_scores(cfg.heads, cfg.blocks, seed=100 + branch)
+        assert sha256_tensor(scores) == str(g[f"{name}_scores_sha{branch}"])
+        r = kernels.route_select(scores.to(DEV), target=cfg.mass_target, keep=cfg.keep,
                                  sink_blocks=cfg.sink_blocks)
         torch.cuda.synchronize()
         check_csr(r, routes[branch])
