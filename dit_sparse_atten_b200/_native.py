@@ -7,6 +7,7 @@ when it is missing or when a call fails; there is no CPU substitute.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -28,6 +29,7 @@ SIGNATURES = {
     "bsa_exact_block_mass": ([_P, _P, _I64, _I64, _I64, _I32, _I32, _F32, _P, _P, _P], _I32),
     "bsa_attention_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _P, _P, _I32,
                            _I32, _I32, _F32, _P, _I64, _I64, _I64, _P, _P, _P], _I32),
+    "bsa_exp2": ([_P, _P, _I64, _I32, _P], _I32),
 }
 
 DEVICE_ERRORS = {
@@ -42,11 +44,17 @@ _err_words: dict = {}
 
 
 def load_library(path: Path | None = None) -> ctypes.CDLL:
-    """Load ``libbsa.so`` once and bind every entry point's signature."""
+    """Load ``libbsa.so`` once and bind every entry point's signature.
+
+    The library next to this file is used unless ``path`` or the environment
+    variable ``BSA_LIBRARY_PATH`` names another build.
+    """
     global _lib
     with _lock:
         if _lib is not None:
             return _lib
+        if path is None and os.environ.get("BSA_LIBRARY_PATH"):
+            path = os.environ["BSA_LIBRARY_PATH"]
         target = Path(path) if path is not None else LIBRARY_PATH
         if not target.exists():
             raise RuntimeError(

@@ -319,4 +319,13 @@ int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
   return ok();
 }
 
+int bsa_exp2(const float* x, float* y, int64_t n, int32_t mode, void* stream) {
+  if (x == nullptr || y == nullptr) return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (mode != 0 && mode != 1) return fail(BSA_ERR_INVALID_ARGUMENT, "mode must be 0 or 1");
+  if (n < 0) return fail(BSA_ERR_INVALID_ARGUMENT, "negative size");
+  cudaError_t e = bsa::launch_exp2(x, y, n, mode, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_exp2 launch");
+  return ok();
+}
+
 }  // extern "C"

@@ -31,6 +31,12 @@ constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of every 8 column pairs of a full key block, this many take their
+// exponentials on the FMA pipe (exp2_poly2) instead of MUFU.
+#ifndef BSA_EMULATED_PAIRS
+#define BSA_EMULATED_PAIRS 2
+#endif
+constexpr int kEmulatedPairsPer8 = BSA_EMULATED_PAIRS;
 
 template <int BK>
 struct AttnLayout {
@@ -253,27 +259,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int x = 0; x < BK; ++x) s[x] = __uint_as_float(r[x]);
         const int kb = block_id(j);
         const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
-        if (valid < BK) {
+        const bool partial = valid < BK;
+        if (partial) {
 #pragma unroll
           for (int x = 0; x < BK; ++x)
             if (x >= valid) s[x] = -INFINITY;
         }
-        float mx = s[0];
+        // Row max in 8 independent three-input chains.
+        float m8[8];
 #pragma unroll
-        for (int x = 1; x < BK; ++x) mx = fmaxf(mx, s[x]);
+        for (int t = 0; t < 8; ++t) m8[t] = fmaxf(s[2 * t], s[2 * t + 1]);
+#pragma unroll
+        for (int x = 16; x < BK; x += 16) {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) m8[t] = fmax3(m8[t], s[x + 2 * t], s[x + 2 * t + 1]);
+        }
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                               fmaxf(m8[6], m8[7]));
         const float mrow = mx * c;
         need = mrow > m_used + kRescaleThreshold;
         const float m_new = need ? mrow : m_used;
         p_scale = need ? ex2_approx(m_used - m_new) : 1.f;
         m_used = m_new;
         l *= p_scale;
-        float rs = 0.f;
+        // p = 2^(s*c - m): packed FMA, MUFU for most columns and the FMA-pipe
+        // polynomial for kEmulated of every 8 column pairs of full blocks;
+        // row sum in 4 independent packed accumulators.
+        const float2 c2 = make_float2(c, c);
+        const float2 neg_m = make_float2(-m_used, -m_used);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        if (partial) {
 #pragma unroll
-        for (int x = 0; x < BK; ++x) {
-          s[x] = ex2_approx(fmaf(s[x], c, -m_used));
-          rs += s[x];
+          for (int x = 0; x < BK; x += 2) {
+            const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
+            s[x] = ex2_approx(t.x);
+            s[x + 1] = ex2_approx(t.y);
+            acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], make_float2(s[x], s[x + 1]));
+          }
+        } else {
+#pragma unroll
+          for (int x = 0; x < BK; x += 2) {
+            const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
+            float2 p;
+            if (((x >> 1) & 7) >= 8 - kEmulatedPairsPer8) {
+              p = exp2_poly2(t);
+            } else {
+              p.x = ex2_approx(t.x);
+              p.y = ex2_approx(t.y);
+            }
+            s[x] = p.x;
+            s[x + 1] = p.y;
+            acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], p);
+          }
         }
-        l += rs;
+        const float2 a01 = __fadd2_rn(acc[0], acc[1]);
+        const float2 a23 = __fadd2_rn(acc[2], acc[3]);
+        const float2 a03 = __fadd2_rn(a01, a23);
+        l += a03.x + a03.y;
       }
       // PV_{j-1} must be complete before P is overwritten or O rescaled.
       if (j > 0) {

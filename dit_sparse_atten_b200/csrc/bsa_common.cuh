@@ -260,6 +260,36 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of values on the FMA pipe (no MUFU), used for a share of the
+// softmax exponentials so the MUFU pipe is not the bottleneck.
+// Method: Cody-Waite split x = n + f with n = rint(x) (the 1.5*2^23 rounding
+// constant), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
+// coefficients were fitted for this kernel with the Remez exchange algorithm
+// (minimax relative error 7.5e-5 on [-1/2, 1/2], far below the 2^-8 rounding
+// of the bf16 probabilities); 2^n is added to the exponent bits.  Inputs are
+// clamped to >= -126, so results below 2^-126 come out as ~2^-126 instead of 0.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(f, make_float2(0.0551716685f, 0.0551716685f),
+                        make_float2(0.2426111251f, 0.2426111251f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  const uint32_t b0 = __float_as_uint(p.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t b1 = __float_as_uint(p.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(b0), __uint_as_float(b1));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

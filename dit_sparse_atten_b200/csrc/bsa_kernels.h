@@ -68,4 +68,7 @@ cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args,
                              cudaStream_t stream);
 
+// ---- diagnostics ------------------------------------------------------------
+cudaError_t launch_exp2(const float* x, float* y, int64_t n, int mode, cudaStream_t stream);
+
 }  // namespace bsa

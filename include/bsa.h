@@ -144,6 +144,15 @@ BSA_API int bsa_attention_fwd(const void* q, const void* k, const void* v, int64
                       void* out, int64_t out_stride_b, int64_t out_stride_t,
                       int64_t out_stride_h, float* lse, int32_t* err_word, void* stream);
 
+/*
+ * Diagnostics: y[i] = 2^x[i] for n float32 values through one of the two
+ * exponential paths of the softmax kernels: mode 0 = the MUFU ex2.approx
+ * instruction, mode 1 = the FMA-pipe polynomial (Cody-Waite split + Remez
+ * degree-3, relative error <= 1e-4 for x >= -126).  No reference
+ * counterpart: it exists so the approximation can be tested on its own.
+ */
+BSA_API int bsa_exp2(const float* x, float* y, int64_t n, int32_t mode, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

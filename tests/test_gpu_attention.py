@@ -153,3 +153,18 @@ def test_config4_720p_layer_morton(golden):
         assert_attention_close(got[rows], ref[rows])
     perm = lay.permutation_cpu.long().to(DEV)
     assert torch.equal(out[:, perm[:512]].view(torch.int16), out_p[:, :512].view(torch.int16))
+
+
+def test_exp2_paths_accuracy():
+    """Both softmax exponentials against float64 and CUDA's exp2f (torch.exp2)."""
+    x = torch.cat([torch.linspace(-126.0, 8.0, 1 << 20), torch.tensor([0.0, -0.5, 0.5, 7.99])])
+    ref = np.exp2(x.double().numpy())
+    xd = x.to(DEV)
+    poly = kernels.exp2(xd, "poly").double().cpu().numpy()
+    mufu = kernels.exp2(xd, "mufu").double().cpu().numpy()
+    cuda_exp2f = torch.exp2(xd).double().cpu().numpy()
+    assert (np.abs(poly - ref) / ref).max() <= 1e-4
+    assert (np.abs(mufu - ref) / ref).max() <= 2.0 ** -21
+    assert (np.abs(poly - cuda_exp2f) / cuda_exp2f).max() <= 1e-4 + 2.0 ** -22
+    below = kernels.exp2(torch.tensor([-200.0, -1000.0], device=DEV), "poly").cpu()
+    assert (below >= 0).all() and (below < 2.0 ** -125).all()

@@ -1,0 +1,111 @@
+"""Head-parallel (Ulysses) exchange and the keep all-reduce on 2 CPU ranks (gloo)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dit_sparse_atten_b200 import parallel
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, fn, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        queue.put((rank, fn(rank, world)))
+    except Exception as exc:  # reported to the parent
+        queue.put((rank, exc))
+    finally:
+        dist.destroy_process_group()
+
+
+def run_ranks(fn, world=2):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fn, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, value in results.items():
+        if isinstance(value, Exception):
+            raise value
+    return results
+
+
+def full_inputs():
+    g = torch.Generator().manual_seed(0)
+    return [torch.randn((1, 64, 4, 8), generator=g) for _ in range(3)]
+
+
+def _exchange(rank, world):
+    q, _, _ = full_inputs()
+    t = q.shape[1] // world
+    shard = q[:, rank * t:(rank + 1) * t]
+    heads = parallel.seq_to_head(shard, dist.group.WORLD, world)
+    hp = q.shape[2] // world
+    assert torch.equal(heads, q[:, :, rank * hp:(rank + 1) * hp])
+    back = parallel.head_to_seq(heads, dist.group.WORLD, world)
+    assert torch.equal(back, shard)
+    return True
+
+
+def _attention(rank, world):
+    q, k, v = full_inputs()
+    t = q.shape[1] // world
+    sl = slice(rank * t, (rank + 1) * t)
+
+    def attend(qh, kh, vh):
+        return torch.nn.functional.scaled_dot_product_attention(
+            qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2)).transpose(1, 2)
+
+    out = parallel.head_parallel_attention(q[:, sl], k[:, sl], v[:, sl], attend,
+                                           dist.group.WORLD, world)
+    ref = attend(q, k, v)[:, sl]
+    torch.testing.assert_close(out, ref)
+    return True
+
+
+def _keep(rank, world):
+    from dit_sparse_atten_b200.flex import FlexReuseBackend
+    backend = FlexReuseBackend(process_group=dist.group.WORLD)
+    kept = torch.tensor([3, 5]) if rank == 0 else torch.tensor([7, 1])
+    return backend._global_keep(kept, 2 * 4 * 4)
+
+
+def test_seq_head_exchange_round_trip():
+    assert all(run_ranks(_exchange).values())
+
+
+def test_head_parallel_attention_equals_full():
+    assert all(run_ranks(_attention).values())
+
+
+def test_keep_fraction_is_global():
+    results = run_ranks(_keep)
+    assert results[0] == results[1] == pytest.approx(16 / 64)
+
+
+def test_plans():
+    p = parallel.make_plan(8, 5, 40, batch=2)
+    assert (p.cfg_groups, p.group_size, p.group_index, p.group_rank) == (2, 4, 1, 1)
+    assert p.head_slice == slice(10, 20) and p.branches(2) == [1]
+    p = parallel.make_plan(2, 1, 40, batch=2)
+    assert p.group_size == 1 and p.branches(2) == [1] and p.head_slice == slice(0, 40)
+    p = parallel.make_plan(1, 0, 40, batch=2)
+    assert p.cfg_groups == 1 and p.branches(2) == [0, 1]
+    p = parallel.make_plan(8, 3, 40, batch=2, split_cfg=False)
+    assert p.group_size == 8 and p.head_slice == slice(15, 20)
+    with pytest.raises(ValueError):
+        parallel.make_plan(3, 0, 40, batch=1)
