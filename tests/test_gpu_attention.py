@@ -163,8 +163,10 @@ def test_exp2_paths_accuracy():
     poly = kernels.exp2(xd, "poly").double().cpu().numpy()
     mufu = kernels.exp2(xd, "mufu").double().cpu().numpy()
     cuda_exp2f = torch.exp2(xd).double().cpu().numpy()
-    assert (np.abs(poly - ref) / ref).max() <= 1e-4
-    assert (np.abs(mufu - ref) / ref).max() <= 2.0 ** -21
-    assert (np.abs(poly - cuda_exp2f) / cuda_exp2f).max() <= 1e-4 + 2.0 ** -22
+    normal = x.numpy() >= -125.0            # results >= 2^-125 stay normal floats
+    assert (np.abs(poly - ref) / ref)[normal].max() <= 1e-4
+    assert np.abs(poly - ref)[~normal].max() <= 2.0 ** -125 * 1e-3
+    assert (np.abs(mufu - ref) / ref)[normal].max() <= 2.0 ** -21
+    assert (np.abs(poly - cuda_exp2f) / cuda_exp2f)[normal].max() <= 1e-4 + 2.0 ** -22
     below = kernels.exp2(torch.tensor([-200.0, -1000.0], device=DEV), "poly").cpu()
     assert (below >= 0).all() and (below < 2.0 ** -125).all()
