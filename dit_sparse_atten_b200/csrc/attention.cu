@@ -14,9 +14,12 @@
 //   warp 5      TMEM allocator and single-thread tcgen05.mma issuer:
 //               S_j = Q K_j^T into one of two TMEM S buffers, O += P_j V_j
 //   warps 0-3   softmax: thread i owns query row i (TMEM lane i); reads S_j,
-//               online max/sum in the log2 domain, writes bf16 P_j to shared
-//               memory (128-byte swizzle), rescales O in TMEM when the running
-//               max grows by more than 2^8, and runs the epilogue.
+//               online max/sum in the log2 domain, writes bf16 P_j to one of
+//               two shared-memory buffers (128-byte swizzle), rescales O in
+//               TMEM when the running max grows by more than 2^8, and runs the
+//               epilogue.  With two P buffers the softmax never waits for the
+//               previous PV unless it rescales, so the MMA queue (PV_{j-1},
+//               S_{j+1}) covers the signalling latency.
 // TMEM columns: S buffers at [0,BK) and [128,128+BK), O at [256,384).
 // Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
 // kErrWaitTimeout in the caller's error word, drains its in-flight copies and
@@ -44,12 +47,12 @@ struct AttnLayout {
   static constexpr int kQBytes = 2 * kPanelRows * 128;   // two 64-column panels
   static constexpr int kSlotPanel = BK * 128;            // one 64-column panel of K or V
   static constexpr int kSlotBytes = 2 * kSlotPanel;
-  static constexpr int kPBytes = (BK / 64) * kPanelRows * 128;
-  static constexpr int kSlots = BK == 128 ? 5 : 8;
+  static constexpr int kPBytes = (BK / 64) * kPanelRows * 128;  // one P buffer
+  static constexpr int kSlots = BK == 128 ? 4 : 8;
   static constexpr int kQOff = 0;
   static constexpr int kRingOff = kQOff + kQBytes;
-  static constexpr int kPOff = kRingOff + kSlots * kSlotBytes;
-  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kPOff = kRingOff + kSlots * kSlotBytes;   // two P buffers
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;  // + alignment slack
 };
@@ -211,7 +214,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t v_addr = ring_addr + s * L::kSlotBytes;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t da = sdesc_sw128(p_addr + (kk >> 2) * (L::kPanelRows * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t da = sdesc_sw128(
+              p_addr + (j & 1) * L::kPBytes + (kk >> 2) * (L::kPanelRows * 128) + (kk & 3) * 32,
+              16, 1024);
           const uint64_t db = sdesc_sw128(v_addr + kk * 16 * 128, L::kSlotPanel, 1024);
           umma_bf16_ss(tmem + 256, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
@@ -318,14 +323,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float2 a03 = __fadd2_rn(a01, a23);
         l += a03.x + a03.y;
       }
-      // PV_{j-1} must be complete before P is overwritten or O rescaled.
-      if (j > 0) {
-        ok = mbar_wait(&bar->o_done, (j - 1) & 1, abort_flag, a.err_word);
-        if (!ok) break;
-        tc_fence_after();
-      }
+      // P_j goes to buffer j&1.  Its previous reader PV_{j-2} was issued before
+      // S_j, so it completed before S_j's commit: no wait.  Only an O rescale
+      // has to wait for PV_{j-1} (O must be stable); with the 2^8 slack that
+      // is rare after the first blocks.
       if (warp_active) {
         if (j > 0 && __any_sync(0xffffffffu, need)) {
+          ok = mbar_wait(&bar->o_done, (j - 1) & 1, abort_flag, a.err_word);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
           for (int cchunk = 0; cchunk < kHeadDim / 32; ++cchunk) {
             uint32_t o[32];
@@ -346,7 +352,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           pk.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
           pk.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
           pk.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
-          uint8_t* dst = sP + (ch >> 3) * (L::kPanelRows * 128) + sw128_offset(row, ch & 7);
+          uint8_t* dst = sP + (j & 1) * L::kPBytes + (ch >> 3) * (L::kPanelRows * 128) +
+                         sw128_offset(row, ch & 7);
           *reinterpret_cast<uint4*>(dst) = pk;
         }
       }
