@@ -36,6 +36,7 @@ DEVICE_ERRORS = {
     1: "a bounded wait inside a kernel timed out",
     2: "a route/permutation entry was out of range",
     4: "tensor-memory allocation failed",
+    8: "the kernel's shared-memory layout did not fit",
 }
 
 _lock = threading.Lock()

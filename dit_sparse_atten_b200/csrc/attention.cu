@@ -9,18 +9,23 @@
 //
 // One CTA handles one (qb, h, b) work item: 128 query rows (the MMA M), key
 // blocks of BK = 128 (or 64) tokens.
-//   warp 4      TMA producer: Q once, then K/V tiles by routed block id into a
+//   warp 8      TMA producer: Q once, then K/V tiles by routed block id into a
 //               ring of shared-memory slots (consumption order K0,K1,V0,K2,V1..)
-//   warp 5      TMEM allocator and single-thread tcgen05.mma issuer:
+//   warp 9      TMEM allocator and single-thread tcgen05.mma issuer:
 //               S_j = Q K_j^T into one of two TMEM S buffers, O += P_j V_j
-//   warps 0-3   softmax: thread i owns query row i (TMEM lane i); reads S_j,
-//               online max/sum in the log2 domain, writes bf16 P_j to one of
-//               two shared-memory buffers (128-byte swizzle), rescales O in
-//               TMEM when the running max grows by more than 2^8, and runs the
-//               epilogue.  With two P buffers the softmax never waits for the
-//               previous PV unless it rescales, so the MMA queue (PV_{j-1},
-//               S_{j+1}) covers the signalling latency.
+//   warps 0-7   softmax.  Warp w owns TMEM lanes 32*(w%4).. (query rows) and
+//               column half w/4 of every S tile and of O.  The two warps of a
+//               row exchange half-row maxima through shared memory (named
+//               barrier 1 + w%4, 64 threads); each keeps its own partial row
+//               sum.  Scores are handled in the log2 domain with a running
+//               stabiliser that only moves when the max grows by more than 2^8
+//               (then O is rescaled in TMEM).  P_j (bf16) goes to one of two
+//               128-byte-swizzled shared-memory buffers; the epilogue
+//               normalises O and stores it.
 // TMEM columns: S buffers at [0,BK) and [128,128+BK), O at [256,384).
+// With two P buffers the softmax never waits for the previous PV unless it
+// rescales O, so the MMA queue (PV_{j-1}, S_{j+1}) covers the signalling
+// latency.
 // Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
 // kErrWaitTimeout in the caller's error word, drains its in-flight copies and
 // MMAs, frees TMEM and exits.
@@ -29,7 +34,10 @@
 namespace bsa {
 namespace {
 
-constexpr int kAttnThreads = 192;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kAttnThreads = 320;
 constexpr int kHeadDim = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -52,9 +60,11 @@ struct AttnLayout {
   static constexpr int kQOff = 0;
   static constexpr int kRingOff = kQOff + kQBytes;
   static constexpr int kPOff = kRingOff + kSlots * kSlotBytes;   // two P buffers
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kXOff = kPOff + 2 * kPBytes;              // half-row exchange
+  static constexpr int kXBytes = 2 * 2 * 128 * 4;                // [parity][half][row] floats
+  static constexpr int kBarOff = kXOff + kXBytes;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kUsed = kBarOff + kBarBytes;
 };
 
 struct AttnBarriers {
@@ -69,19 +79,33 @@ struct AttnBarriers {
   int abort;
 };
 
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// bf16x2 from two floats, round half away from zero on the magnitude (integer
+// ALU instead of the conversion unit, which the exponentials also use).
+__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
+
 template <int BK>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     bsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
   using L = AttnLayout<BK>;
+  constexpr int HC = BK / 2;  // S columns per softmax half
   static_assert(sizeof(AttnBarriers) <= L::kBarBytes, "barrier area");
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sRing = smem + L::kRingOff;
   uint8_t* sP = smem + L::kPOff;
+  float* sX = reinterpret_cast<float*>(smem + L::kXOff);
   AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(smem + L::kBarOff);
   volatile int* abort_flag = &bar->abort;
 
@@ -100,17 +124,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 
   if (threadIdx.x == 0) {
+    uint32_t dyn_bytes;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_bytes));
+    const bool fits = (smem - smem_raw) + L::kUsed <= static_cast<int>(dyn_bytes);
     mbar_init(&bar->q_full, 1);
     mbar_init(&bar->s_full[0], 1);
     mbar_init(&bar->s_full[1], 1);
-    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->p_full, kSoftmaxWarps * 32);
     mbar_init(&bar->o_done, 1);
     mbar_init(&bar->drain, 1);
     for (int s = 0; s < L::kSlots; ++s) {
       mbar_init(&bar->slot_full[s], 1);
       mbar_init(&bar->slot_empty[s], 1);
     }
-    bar->abort = prior_timeout(a.err_word) ? 1 : 0;
+    bar->abort = (prior_timeout(a.err_word) || !fits) ? 1 : 0;
+    if (!fits) atomicOr(a.err_word, kErrSmemLayout);
     fence_mbar_init();
   }
   __syncthreads();
@@ -125,7 +153,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     fence_proxy_async_smem();
   }
-  if (warp == 5) tmem_alloc(&bar->tmem_base, 512);
+  if (warp == kMmaWarp) tmem_alloc(&bar->tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -140,7 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     return kb;
   };
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm_q);
@@ -176,7 +204,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int s = 0; s < L::kSlots; ++s)
         if (armed[s] < 2) mbar_wait(&bar->slot_full[s], armed[s], &never, a.err_word);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, BK, false);
@@ -196,7 +224,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
           const uint32_t off = (kk & 3) * 32;
-          const uint64_t da = sdesc_sw128(q_addr + (kk >> 2) * (L::kPanelRows * 128) + off, 16, 1024);
+          const uint64_t da =
+              sdesc_sw128(q_addr + (kk >> 2) * (L::kPanelRows * 128) + off, 16, 1024);
           const uint64_t db = sdesc_sw128(k_addr + (kk >> 2) * L::kSlotPanel + off, 16, 1024);
           umma_bf16_ss(d, da, db, idesc_s, kk > 0 ? 1u : 0u);
         }
@@ -237,66 +266,74 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    const bool warp_active = (BK == 128) || (warp < 2);
+    const int half = warp >> 2;                // column half of S and O
+    const int wq = warp & 3;                   // TMEM lane quarter
+    const int row = wq * 32 + lane;            // query row == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t pair_barrier = 1 + wq;      // the two warps sharing these lanes
+    const bool warp_active = (BK == 128) || (wq < 2);
     const int64_t token = static_cast<int64_t>(qb) * BK + row;
     const bool row_valid = warp_active && row < BK && token < a.tokens;
     const float c = a.scale * kLog2e;
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
+    int kb_next = (warp_active && n > 0) ? block_id(0) : 0;
     for (int j = 0; ok && j < n; ++j) {
       ok = mbar_wait(&bar->s_full[j & 1], (j >> 1) & 1, abort_flag, a.err_word);
       if (!ok) break;
       tc_fence_after();
-      float s[BK];
+      float s[HC];
       float p_scale = 1.f;
       bool need = false;
       if (warp_active) {
-        uint32_t r[BK];
+        const int kb = kb_next;
+        if (j + 1 < n) kb_next = block_id(j + 1);  // hide the next id's load latency
+        uint32_t r[HC];
 #pragma unroll
-        for (int cchunk = 0; cchunk < BK / 32; ++cchunk)
-          tmem_ld_32x32b_x32(tmem + lane_addr + (j & 1) * 128 + cchunk * 32, r + cchunk * 32);
+        for (int cc = 0; cc < HC / 32; ++cc)
+          tmem_ld_32x32b_x32(tmem + lane_addr + (j & 1) * 128 + half * HC + cc * 32, r + cc * 32);
         tmem_wait_ld();
-        reg_fence<BK>(r);
+        reg_fence<HC>(r);
 #pragma unroll
-        for (int x = 0; x < BK; ++x) s[x] = __uint_as_float(r[x]);
-        const int kb = block_id(j);
-        const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
-        const bool partial = valid < BK;
+        for (int x = 0; x < HC; ++x) s[x] = __uint_as_float(r[x]);
+        const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK - half * HC;
+        const bool partial = valid < HC;
         if (partial) {
 #pragma unroll
-          for (int x = 0; x < BK; ++x)
+          for (int x = 0; x < HC; ++x)
             if (x >= valid) s[x] = -INFINITY;
         }
-        // Row max in 8 independent three-input chains.
+        // Half-row max in 8 independent three-input chains, then the pair's max.
         float m8[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) m8[t] = fmaxf(s[2 * t], s[2 * t + 1]);
 #pragma unroll
-        for (int x = 16; x < BK; x += 16) {
+        for (int x = 16; x < HC; x += 16) {
 #pragma unroll
           for (int t = 0; t < 8; ++t) m8[t] = fmax3(m8[t], s[x + 2 * t], s[x + 2 * t + 1]);
         }
-        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+        const float mh = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
                                fmaxf(m8[6], m8[7]));
-        const float mrow = mx * c;
+        float* xs = sX + (j & 1) * 256;
+        xs[half * 128 + row] = mh;
+        named_bar_sync(pair_barrier, 64);
+        const float mrow = fmaxf(mh, xs[(half ^ 1) * 128 + row]) * c;
         need = mrow > m_used + kRescaleThreshold;
         const float m_new = need ? mrow : m_used;
         p_scale = need ? ex2_approx(m_used - m_new) : 1.f;
         m_used = m_new;
         l *= p_scale;
-        // p = 2^(s*c - m): packed FMA, MUFU for most columns and the FMA-pipe
-        // polynomial for kEmulated of every 8 column pairs of full blocks;
-        // row sum in 4 independent packed accumulators.
+        // p = 2^(s*c - m): packed FMA; MUFU for most columns and the FMA-pipe
+        // polynomial for kEmulatedPairsPer8 of every 8 column pairs of full
+        // blocks; partial sums in 4 independent packed accumulators.
         const float2 c2 = make_float2(c, c);
         const float2 neg_m = make_float2(-m_used, -m_used);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
         if (partial) {
 #pragma unroll
-          for (int x = 0; x < BK; x += 2) {
+          for (int x = 0; x < HC; x += 2) {
             const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
             s[x] = ex2_approx(t.x);
             s[x + 1] = ex2_approx(t.y);
@@ -304,7 +341,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         } else {
 #pragma unroll
-          for (int x = 0; x < BK; x += 2) {
+          for (int x = 0; x < HC; x += 2) {
             const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
             float2 p;
             if (((x >> 1) & 7) >= 8 - kEmulatedPairsPer8) {
@@ -318,24 +355,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], p);
           }
         }
-        const float2 a01 = __fadd2_rn(acc[0], acc[1]);
-        const float2 a23 = __fadd2_rn(acc[2], acc[3]);
-        const float2 a03 = __fadd2_rn(a01, a23);
+        const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
         l += a03.x + a03.y;
       }
       // P_j goes to buffer j&1.  Its previous reader PV_{j-2} was issued before
       // S_j, so it completed before S_j's commit: no wait.  Only an O rescale
-      // has to wait for PV_{j-1} (O must be stable); with the 2^8 slack that
-      // is rare after the first blocks.
+      // has to wait for PV_{j-1} (O must be stable); with the 2^8 slack that is
+      // rare after the first blocks.
       if (warp_active) {
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           ok = mbar_wait(&bar->o_done, (j - 1) & 1, abort_flag, a.err_word);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
-          for (int cchunk = 0; cchunk < kHeadDim / 32; ++cchunk) {
+          for (int cc = 0; cc < kHeadDim / 64; ++cc) {
             uint32_t o[32];
-            const uint32_t addr = tmem + lane_addr + 256 + cchunk * 32;
+            const uint32_t addr = tmem + lane_addr + 256 + half * 64 + cc * 32;
             tmem_ld_32x32b_x32(addr, o);
             tmem_wait_ld();
             reg_fence<32>(o);
@@ -345,15 +380,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             tmem_wait_st();
           }
         }
+        // This half's columns of P: 8-key chunks into the 128-byte swizzle.
+        uint8_t* pbuf = sP + (j & 1) * L::kPBytes;
 #pragma unroll
-        for (int ch = 0; ch < BK / 8; ++ch) {
+        for (int ch = 0; ch < HC / 8; ++ch) {
+          const int gch = half * (HC / 8) + ch;  // chunk index within the BK-key row
           uint4 pk;
-          pk.x = pack_bf16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
-          pk.y = pack_bf16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
-          pk.z = pack_bf16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
-          pk.w = pack_bf16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
-          uint8_t* dst = sP + (j & 1) * L::kPBytes + (ch >> 3) * (L::kPanelRows * 128) +
-                         sw128_offset(row, ch & 7);
+          pk.x = pack_bf16x2_alu(s[ch * 8 + 0], s[ch * 8 + 1]);
+          pk.y = pack_bf16x2_alu(s[ch * 8 + 2], s[ch * 8 + 3]);
+          pk.z = pack_bf16x2_alu(s[ch * 8 + 4], s[ch * 8 + 5]);
+          pk.w = pack_bf16x2_alu(s[ch * 8 + 6], s[ch * 8 + 7]);
+          uint8_t* dst = pbuf + (gch >> 3) * (L::kPanelRows * 128) + sw128_offset(row, gch & 7);
           *reinterpret_cast<uint4*>(dst) = pk;
         }
       }
@@ -367,13 +404,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
     }
     if (warp_active) {
-      __nv_bfloat16* out = a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h;
-      const float inv_l = (n > 0 && l > 0.f) ? 1.f / l : 0.f;
+      // Row sum = both halves' partial sums.
+      float* xs = sX + (n & 1) * 256;
+      xs[half * 128 + row] = l;
+      named_bar_sync(pair_barrier, 64);
+      const float l_row = l + xs[(half ^ 1) * 128 + row];
+      __nv_bfloat16* out =
+          a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h + half * 64;
+      const float inv_l = (n > 0 && l_row > 0.f) ? 1.f / l_row : 0.f;
 #pragma unroll
-      for (int cchunk = 0; cchunk < kHeadDim / 32; ++cchunk) {
+      for (int cc = 0; cc < kHeadDim / 64; ++cc) {
         uint32_t o[32];
         if (ok && n > 0) {
-          tmem_ld_32x32b_x32(tmem + lane_addr + 256 + cchunk * 32, o);
+          tmem_ld_32x32b_x32(tmem + lane_addr + 256 + half * 64 + cc * 32, o);
           tmem_wait_ld();
           reg_fence<32>(o);
         } else {
@@ -384,23 +427,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * inv_l, __uint_as_float(o[v4 * 8 + 1]) * inv_l);
-            pk.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * inv_l, __uint_as_float(o[v4 * 8 + 3]) * inv_l);
-            pk.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * inv_l, __uint_as_float(o[v4 * 8 + 5]) * inv_l);
-            pk.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * inv_l, __uint_as_float(o[v4 * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(out + cchunk * 32 + v4 * 8) = pk;
+            pk.x = pack_bf16x2(__uint_as_float(o[v4 * 8 + 0]) * inv_l,
+                               __uint_as_float(o[v4 * 8 + 1]) * inv_l);
+            pk.y = pack_bf16x2(__uint_as_float(o[v4 * 8 + 2]) * inv_l,
+                               __uint_as_float(o[v4 * 8 + 3]) * inv_l);
+            pk.z = pack_bf16x2(__uint_as_float(o[v4 * 8 + 4]) * inv_l,
+                               __uint_as_float(o[v4 * 8 + 5]) * inv_l);
+            pk.w = pack_bf16x2(__uint_as_float(o[v4 * 8 + 6]) * inv_l,
+                               __uint_as_float(o[v4 * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(out + cc * 32 + v4 * 8) = pk;
           }
         }
       }
-      if (row_valid && a.lse != nullptr) {
+      if (row_valid && half == 0 && a.lse != nullptr) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
-            (n > 0 && l > 0.f) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
+            (n > 0 && l_row > 0.f) ? (m_used + __log2f(l_row)) * kLn2 : -INFINITY;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -410,19 +457,27 @@ template <int BK>
 cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                       const AttnArgs& a, cudaStream_t stream) {
   using L = AttnLayout<BK>;
-  static bool configured[64] = {};
+  // The layout needs kUsed bytes from a 1024-byte-aligned base; ask for up to
+  // 1 KB of slack within the opt-in limit (the kernel checks and reports).
+  static int smem_bytes[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(bsa_attention_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             L::kSmemBytes);
+  int bytes = (dev >= 0 && dev < 64) ? smem_bytes[dev] : 0;
+  if (bytes == 0) {
+    int optin = 0;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    bytes = optin < L::kUsed + 1024 ? optin : L::kUsed + 1024;
+    if (bytes < L::kUsed) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(bsa_attention_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             bytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) smem_bytes[dev] = bytes;
   }
   const dim3 grid(static_cast<unsigned>(a.q_blocks), static_cast<unsigned>(a.heads),
                   static_cast<unsigned>(a.batch));
-  bsa_attention_kernel<BK><<<grid, kAttnThreads, L::kSmemBytes, stream>>>(tq, tk, tv, a);
+  bsa_attention_kernel<BK><<<grid, kAttnThreads, bytes, stream>>>(tq, tk, tv, a);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,7 @@ enum DeviceError : int {
   kErrWaitTimeout = 1 << 0,   // an mbarrier wait exceeded its time limit
   kErrBadRoute = 1 << 1,      // a CSR count/index was out of range (skipped)
   kErrTmemAlloc = 1 << 2,     // TMEM allocation returned an unexpected address
+  kErrSmemLayout = 1 << 3,    // the dynamic shared memory cannot hold the kernel's layout
 };
 
 // A wait on an mbarrier gives up after this many nanoseconds; the kernel then

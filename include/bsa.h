@@ -42,6 +42,7 @@ extern "C" {
 #define BSA_DEVICE_WAIT_TIMEOUT 1 /* a bounded mbarrier wait gave up */
 #define BSA_DEVICE_BAD_ROUTE 2    /* a CSR count / block id / permutation entry was out of range */
 #define BSA_DEVICE_TMEM_ALLOC 4   /* tensor-memory allocation returned an unusable address */
+#define BSA_DEVICE_SMEM_LAYOUT 8  /* the dynamic shared memory could not hold the kernel's layout */
 
 /* Library version, major*10000 + minor*100 + patch. */
 BSA_API int bsa_version(void);
