@@ -307,6 +307,10 @@ int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
   a.route_batch_stride = route_has_batch ? 1 : 0;
   a.counts = counts;
   a.indices = indices;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.in_stride_b = in_stride_b;
+  a.in_stride_t = in_stride_t;
+  a.in_stride_h = in_stride_h;
   a.scale = scale;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.out_stride_b = out_stride_b;

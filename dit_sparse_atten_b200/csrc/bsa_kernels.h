@@ -58,6 +58,8 @@ struct AttnArgs {
   int64_t route_batch_stride;     // in rows of [H * Qb]; 0 = one route for all batches
   const int32_t* counts;          // [RB, H, Qb]
   const int32_t* indices;         // [RB, H, Qb, route_cols]
+  const __nv_bfloat16* q;         // [B, T, H, D] with the input strides below (elements)
+  int64_t in_stride_b, in_stride_t, in_stride_h;
   float scale;
   __nv_bfloat16* out;             // [B, T, H, D] with strides below (elements)
   int64_t out_stride_b, out_stride_t, out_stride_h;
