@@ -11,9 +11,13 @@
 // blocks of BK = 128 (or 64) tokens.
 //   warp 8      TMA producer: K/V tiles by routed block id into a ring of
 //               shared-memory slots (consumption order K0, K1, V0, K2, V1, ...)
-//   warp 9      TMEM allocator and single-thread tcgen05.mma issuer:
-//               S_j = Q K_j^T and O += P_j V_j, both with the A operand (Q, P)
-//               in tensor memory and B (K, V) in shared memory
+//   warp 9      TMEM allocator; one thread issues S_j = Q K_j^T
+//   warp 10     one thread issues O += P_j V_j
+//               Both MMAs take A (Q, P) from tensor memory and B (K, V) from
+//               shared memory.  Two issuing threads keep the tensor pipe fed
+//               while either waits on a barrier (the pipe queues only about
+//               one 128x128x16 MMA ahead); descriptors are precomputed so
+//               consecutive MMAs issue back to back.
 //   warps 0-7   softmax.  Warp w owns TMEM lanes 32*(w%4).. (query rows) and
 //               column half w/4 of Q, of every S tile and of O.  They first
 //               copy their Q rows from global memory into TMEM.  The two warps
@@ -27,8 +31,10 @@
 // TMEM columns: S (and P) buffers at [0,128) and [128,256), O at [256,384),
 // Q at [384,448).  Shared memory holds only K/V tiles, so per key block the
 // tensor pipe reads 64 KB from it and TMA writes 64 KB.
-// Ordering: S_{j+2} (which overwrites P_j) is issued after PV_j by the same
-// thread; the softmax never waits for the previous PV unless it rescales O.
+// Ordering: S_{j+2} overwrites P_j, so the S issuer waits for PV_j (o_done);
+// the softmax never waits for the previous PV unless it rescales O.  p_full
+// and o_done alternate between two barriers by block parity so no waiter can
+// fall two phases behind.
 // Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
 // kErrWaitTimeout in the caller's error word, drains its in-flight copies and
 // MMAs, frees TMEM and exits.
@@ -39,8 +45,9 @@ namespace {
 
 constexpr int kSoftmaxWarps = 8;
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kAttnThreads = 320;
+constexpr int kMmaWarp = 9;      // S issuer, TMEM owner
+constexpr int kPvWarp = 10;      // PV issuer
+constexpr int kAttnThreads = 352;
 constexpr int kHeadDim = 128;
 constexpr uint32_t kTmemO = 256;
 constexpr uint32_t kTmemQ = 384;
@@ -70,9 +77,9 @@ struct AttnLayout {
 struct AttnBarriers {
   uint64_t q_full;
   uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t o_done;
-  uint64_t drain;
+  uint64_t p_full[2];
+  uint64_t o_done[2];
+  uint64_t drain[2];
   uint64_t slot_full[8];
   uint64_t slot_empty[8];
   uint32_t tmem_base;
@@ -138,9 +145,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(&bar->q_full, kSoftmaxWarps * 32);
     mbar_init(&bar->s_full[0], 1);
     mbar_init(&bar->s_full[1], 1);
-    mbar_init(&bar->p_full, kSoftmaxWarps * 32);
-    mbar_init(&bar->o_done, 1);
-    mbar_init(&bar->drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->p_full[i], kSoftmaxWarps * 32);
+      mbar_init(&bar->o_done[i], 1);
+      mbar_init(&bar->drain[i], 1);
+    }
     for (int s = 0; s < L::kSlots; ++s) {
       mbar_init(&bar->slot_full[s], 1);
       mbar_init(&bar->slot_empty[s], 1);
@@ -197,59 +206,62 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int s = 0; s < L::kSlots; ++s)
         if (armed[s] < 2) mbar_wait(&bar->slot_full[s], armed[s], &never, a.err_word);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n > 0) {
+  } else if (warp == kMmaWarp || warp == kPvWarp) {
+    // ------------------------------------------------------------ MMA issuers
+    // Load sequence of the producer: K0, then K_{j+1}, V_j for every j.
+    auto seq_k = [](int j) { return j == 0 ? 0 : 2 * j - 1; };
+    auto seq_v = [n](int j) { return j + 1 < n ? 2 * j + 2 : 2 * j + 1; };
+    const uint32_t ring_addr = smem_u32(sRing);
+    if (warp == kMmaWarp && lane == 0 && n > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, BK, false);
-      const uint32_t idesc_o = idesc_bf16_f32(128, kHeadDim, true);
-      const uint32_t ring_addr = smem_u32(sRing);
-      int seq = 0;
+      const uint64_t kdesc0 = sdesc_sw128(ring_addr, 16, 1024);
       bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
-      auto issue_s = [&](int j) {
-        const int s = seq % L::kSlots;
-        const uint32_t ph = (seq / L::kSlots) & 1;
-        if (!mbar_wait(&bar->slot_full[s], ph, abort_flag, a.err_word)) return false;
+      for (int j = 0; ok && j < n; ++j) {
+        const int sq = seq_k(j);
+        const int s = sq % L::kSlots;
+        ok = mbar_wait(&bar->slot_full[s], (sq / L::kSlots) & 1, abort_flag, a.err_word);
+        // S_j overwrites P_{j-2} (same TMEM buffer): PV_{j-2} must be done.
+        if (ok && j >= 2)
+          ok = mbar_wait(&bar->o_done[j & 1], ((j - 2) >> 1) & 1, abort_flag, a.err_word);
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t k_addr = ring_addr + s * L::kSlotBytes;
+        const uint64_t kd = kdesc0 + static_cast<uint64_t>((s * L::kSlotBytes) >> 4);
         const uint32_t d = tmem + (j & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint64_t db =
-              sdesc_sw128(k_addr + (kk >> 2) * L::kSlotPanel + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = kd + static_cast<uint64_t>(((kk >> 2) * L::kSlotPanel + (kk & 3) * 32) >> 4);
           umma_bf16_ts(d, tmem + kTmemQ + kk * 8, db, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar->s_full[j & 1]);
         umma_commit(&bar->slot_empty[s]);
-        ++seq;
-        return true;
-      };
-      auto issue_pv = [&](int j) {
-        const int s = seq % L::kSlots;
-        const uint32_t ph = (seq / L::kSlots) & 1;
-        if (!mbar_wait(&bar->slot_full[s], ph, abort_flag, a.err_word)) return false;
-        if (!mbar_wait(&bar->p_full, j & 1, abort_flag, a.err_word)) return false;
+      }
+      int never = 0;
+      umma_commit(&bar->drain[0]);
+      mbar_wait(&bar->drain[0], 0, &never, a.err_word);
+    } else if (warp == kPvWarp && lane == 0 && n > 0) {
+      const uint32_t idesc_o = idesc_bf16_f32(128, kHeadDim, true);
+      const uint64_t vdesc0 = sdesc_sw128(ring_addr, L::kSlotPanel, 1024);
+      bool ok = true;
+      for (int j = 0; ok && j < n; ++j) {
+        const int sq = seq_v(j);
+        const int s = sq % L::kSlots;
+        ok = mbar_wait(&bar->slot_full[s], (sq / L::kSlots) & 1, abort_flag, a.err_word);
+        if (ok) ok = mbar_wait(&bar->p_full[j & 1], (j >> 1) & 1, abort_flag, a.err_word);
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t v_addr = ring_addr + s * L::kSlotBytes;
+        const uint64_t vd = vdesc0 + static_cast<uint64_t>((s * L::kSlotBytes) >> 4);
+        const uint32_t pa = tmem + (j & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t db = sdesc_sw128(v_addr + kk * 16 * 128, L::kSlotPanel, 1024);
-          umma_bf16_ts(tmem + kTmemO, tmem + (j & 1) * 128 + kk * 8, db, idesc_o,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + kTmemO, pa + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4),
+                       idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(&bar->o_done[j & 1]);
         umma_commit(&bar->slot_empty[s]);
-        umma_commit(&bar->o_done);
-        ++seq;
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
       }
-      // Wait for every issued MMA before TMEM is released.
       int never = 0;
-      umma_commit(&bar->drain);
-      mbar_wait(&bar->drain, 0, &never, a.err_word);
+      umma_commit(&bar->drain[1]);
+      mbar_wait(&bar->drain[1], 0, &never, a.err_word);
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -380,7 +392,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // Only an O rescale has to wait for PV_{j-1} (O must be stable); with
         // the 2^8 slack that is rare after the first blocks.
         if (j > 0 && __any_sync(0xffffffffu, need)) {
-          ok = mbar_wait(&bar->o_done, (j - 1) & 1, abort_flag, a.err_word);
+          ok = mbar_wait(&bar->o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err_word);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
@@ -404,11 +416,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_wait_st();
       }
       tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      mbar_arrive(&bar->p_full[j & 1]);
     }
     // ---------------------------------------------------------- epilogue
     if (ok && n > 0) {
-      ok = mbar_wait(&bar->o_done, (n - 1) & 1, abort_flag, a.err_word);
+      ok = mbar_wait(&bar->o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, a.err_word);
       tc_fence_after();
     }
     if (warp_active) {
