@@ -37,8 +37,11 @@ REPO = Path(__file__).resolve().parent
 METRIC = "Wan-14B 57.6k-token sparse attn layer ms & eff. TFLOPS; 5-step forward sec"
 UNIT = "TFLOPS"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch (ncu), or None.
-ATTENTION_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch per
+# (branch, head) it processes: ncu capture of the 4-head config-4 case (2 branches,
+# 389.1 MB read + 107.0 MB written) divided by 8; traffic grows with the heads
+# processed, so a launch's traffic is this times its branches x heads.
+ATTENTION_TRAFFIC_PER_BRANCH_HEAD = (389.1e6 + 107.0e6) / 8
 
 
 def parse_args(argv=None):
@@ -355,7 +358,8 @@ def main(argv=None):
     achieved = local_flops / (attn_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"],
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops_sustained"],
-                "traffic": ATTENTION_TRAFFIC_BYTES,
+                "traffic": ATTENTION_TRAFFIC_PER_BRANCH_HEAD * local_route.shape[0] * local_route.shape[1],
+                "traffic_source": "ncu dram bytes of the 4-head case, scaled by branches x heads",
                 "peak_source": f"bf16_tflops_sustained ({peak_src})",
                 "frac_of_burst": achieved / peaks["bf16_tflops"],
                 "kernel": "bsa_attention_kernel<128>", "kernel_ms": attn_ms,

@@ -101,6 +101,34 @@ def test_empty_rows_are_zero_and_lse():
     assert (out[0, 128:256, 0] == 0).all()
 
 
+def test_many_items_per_cta_with_empty_rows():
+    """More (b, h, qb) work items than query tiles in flight on the GPU (each
+    persistent CTA walks several), empty routes among them, a partial tail."""
+    g = torch.Generator().manual_seed(9)
+    B, H, T = 2, 4, 128 * 100 - 5
+    blocks = math.ceil(T / 128)
+    q, k, v = (torch.randn((B, T, H, 128), generator=g).to(torch.bfloat16) for _ in range(3))
+    route = torch.rand((B, H, blocks, blocks), generator=g) < 0.08
+    route[..., 0] = True
+    empty = torch.rand((B, H, blocks), generator=g) < 0.1
+    route[empty] = False
+    counts, indices = kernels.pack_boolean_rows(route.to(DEV))
+    out, lse = kernels.block_sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), counts, indices,
+                                              block=128, return_lse=True)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    for b in range(B):
+        ref, ref_lse = oatt.block_sparse_attention(
+            q[b].float().numpy(), k[b].float().numpy(), v[b].float().numpy(),
+            route[b].numpy(), 128, return_lse=True)
+        assert_attention_close(out[b].float().cpu().numpy(), ref)
+        lse_got = lse[b].cpu().numpy()
+        finite = np.isfinite(ref_lse)
+        np.testing.assert_allclose(lse_got[finite], ref_lse[finite], atol=2e-2, rtol=1e-3)
+        assert np.isneginf(lse_got[~finite]).all()
+    assert empty.any()
+
+
 def test_shared_route_across_batch():
     g = torch.Generator().manual_seed(8)
     q, k, v = (torch.randn((2, 512, 2, 128), generator=g).to(torch.bfloat16) for _ in range(3))
