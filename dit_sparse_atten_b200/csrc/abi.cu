@@ -1,6 +1,7 @@
 // C ABI of libbsa.so (declared in include/bsa.h): argument validation, TMA
 // tensor-map encoding and kernel launch.  No entry point allocates memory or
 // synchronises the stream.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -221,6 +222,99 @@ int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch
   a.err_word = err_word;
   cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass launch");
+  return ok();
+}
+
+int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_t tokens,
+                             int64_t heads, int32_t head_dim, int32_t block, int32_t samples,
+                             float scale, int32_t round_bf16, float* mass, int32_t* err_word,
+                             void* stream) {
+  if (q == nullptr || k == nullptr || mass == nullptr || err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (block != 32 && block != 64 && block != 128)
+    return fail(BSA_ERR_UNSUPPORTED, "block must be 32, 64 or 128 (got %d)", block);
+  if (samples != 1 && samples != 2 && samples != 4 && samples != 8 && samples != 16 &&
+      samples != 32)
+    return fail(BSA_ERR_UNSUPPORTED, "samples must be a power of two <= 32 (got %d)", samples);
+  if (samples > block)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "samples (%d) exceed the block (%d)", samples, block);
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/tokens/heads");
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k) & 15))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "q and k must be 16-byte aligned");
+  const int64_t q_blocks = (tokens + block - 1) / block;
+  if (q_blocks > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "q_blocks must be in [1, 4096] (got %lld)",
+                static_cast<long long>(q_blocks));
+  const int64_t n_rows = q_blocks * samples;
+  const int64_t bias_bytes = ((q_blocks * 4 + 255) / 256) * 256;
+  const int64_t per_head = 2 * n_rows * head_dim * 2;
+  const int64_t room = static_cast<int64_t>(bsa::kNoAllocScratchBytes) - bias_bytes;
+  if (per_head > room)
+    return fail(BSA_ERR_UNSUPPORTED,
+                "%lld sampled rows need %lld scratch bytes per head; the static scratch holds "
+                "%lld",
+                static_cast<long long>(n_rows), static_cast<long long>(per_head + bias_bytes),
+                static_cast<long long>(bsa::kNoAllocScratchBytes));
+  const int64_t hc_max = room / per_head;
+  // Scratch address, looked up once per device with that device current.
+  static void* scratch_of[64] = {};
+  static std::mutex scratch_mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(BSA_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(scratch_mu);
+    if (scratch_of[dev] == nullptr) {
+      e = bsa::noalloc_scratch(&scratch_of[dev]);
+      if (e != cudaSuccess) {
+        scratch_of[dev] = nullptr;
+        return cuda_fail(e, "bsa_sampled_mass_noalloc: cudaGetSymbolAddress");
+      }
+    }
+    scratch = scratch_of[dev];
+  }
+  // Key-block weights log(size / S) of flex.py:236-237 (full blocks, last block).
+  const int64_t tail = tokens - (q_blocks - 1) * block;
+  const float bias_full = logf(static_cast<float>(block) / static_cast<float>(samples));
+  const float bias_tail = logf(static_cast<float>(tail) / static_cast<float>(samples));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  for (int64_t b = 0; b < batch; ++b) {
+    for (int64_t h0 = 0; h0 < heads; h0 += hc_max) {
+      const int64_t hc = heads - h0 < hc_max ? heads - h0 : hc_max;
+      const int64_t region = n_rows * hc * head_dim * 2;
+      e = bsa::launch_gather_samples(q, k, tokens, heads, static_cast<int>(b),
+                                     static_cast<int>(h0), static_cast<int>(hc), block, samples,
+                                     static_cast<int>(q_blocks), bias_full, bias_tail, scratch, st);
+      if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_noalloc gather launch");
+      CUtensorMap tq, tk;
+      bool tm = false;
+      int rc = encode_bhtd(&tq, base, 1, n_rows, hc, head_dim, n_rows * hc * head_dim,
+                           hc * head_dim, head_dim, 128, &tm);
+      if (rc != BSA_OK) return rc;
+      rc = encode_bhtd(&tk, base + region, 1, n_rows, hc, head_dim, n_rows * hc * head_dim,
+                       hc * head_dim, head_dim, 128, &tm);
+      if (rc != BSA_OK) return rc;
+      bsa::MassArgs a{};
+      a.batch = 1;
+      a.heads = hc;
+      a.n_rows = n_rows;
+      a.samples = samples;
+      a.q_blocks = static_cast<int32_t>(q_blocks);
+      a.scale = scale;
+      a.round_bf16 = round_bf16;
+      a.block_bias = reinterpret_cast<const float*>(base + 2 * region);
+      a.mass_scale = 1.0f / static_cast<float>(samples);
+      a.mass = mass + (b * heads + h0) * q_blocks * q_blocks;
+      a.err_word = err_word;
+      e = bsa::launch_sampled_mass(tq, tk, a, st);
+      if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_noalloc mass launch");
+    }
+  }
   return ok();
 }
 

@@ -49,6 +49,22 @@ struct MassArgs {
 cudaError_t launch_sampled_mass(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                                 const MassArgs& args, cudaStream_t stream);
 
+// ---- (b) sampled block mass without a caller workspace ---------------------
+// Size of the module-level scratch (a static __device__ array) that
+// bsa_sampled_mass_noalloc gathers a chunk of heads' sampled Q/K rows and the
+// key-block weights into: 2 * N * hc * 256 bytes + Qb * 4 for N = Qb * S
+// sampled rows and hc heads per chunk.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+// Address of that scratch on the current device.
+cudaError_t noalloc_scratch(void** ptr);
+// Gathers the S sampled tokens of every block of heads [h0, h0 + hc) of batch
+// element b of q and k (bf16 [B, T, H, 128] contiguous) into the scratch as
+// [N, hc, 128] each, followed by the Qb key-block weights.
+cudaError_t launch_gather_samples(const void* q, const void* k, int64_t T, int64_t H, int b,
+                                  int h0, int hc, int block, int samples, int q_blocks,
+                                  float bias_full, float bias_tail, void* scratch,
+                                  cudaStream_t stream);
+
 // ---- (a) block-sparse attention --------------------------------------------
 struct AttnArgs {
   int64_t batch, tokens, heads;

@@ -112,6 +112,28 @@ BSA_API int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64
                      int32_t* err_word, void* stream);
 
 /*
+ * (b) Sampled block mass with no caller workspace; it allocates nothing.
+ * No counterpart in the reference: it is bsa_sampled_mass for callers that
+ * have no device allocator to take the sampled-row workspace from (a C or C++
+ * host binding libbsa.so without PyTorch).  q, k: bf16 [batch, tokens, heads,
+ * head_dim] contiguous; mass as bsa_sampled_mass.  The sample rows are gathered
+ * from q and k (flex.py:222-231) into a 32 MiB static device scratch of the
+ * library, a chunk of heads at a time; each head needs
+ * 2 * q_blocks * samples * 256 bytes of it plus 4 * q_blocks, and larger
+ * sizes are rejected with BSA_ERR_UNSUPPORTED.  Nothing has to be zeroed.
+ * Calls on one device share the scratch: two calls must not be in flight at
+ * the same time (on different streams or threads) or they race.  The first
+ * call on a device looks up the scratch address (cudaGetSymbolAddress) and
+ * configures the kernels, so make it before any stream capture.
+ * Same limits as bsa_sampled_mass (samples in {1,...,32}, head_dim == 128,
+ * q_blocks <= 4096) and block in {32, 64, 128}.
+ */
+BSA_API int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_t tokens,
+                                     int64_t heads, int32_t head_dim, int32_t block,
+                                     int32_t samples, float scale, int32_t round_bf16, float* mass,
+                                     int32_t* err_word, void* stream);
+
+/*
  * (b) Exact dense block mass (the exact bootstrap / refresh route source):
  *   mass[b, h, qb, kb] = sum_{q in qb, k in kb, q,k < tokens} softmax_q(k)
  * over full-precision scores (no bf16 rounding) of q, k: bf16 [batch, tokens,
