@@ -180,7 +180,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      uint32_t armed[L::kSlots];
+      // Per slot: a load was issued / its parity (bit masks: a run-time
+      // indexed array would live in local memory, whose traffic slows TMA).
+      uint32_t armed = 0, armed_phase = 0;
       int seq = 0;
       bool ok = true;
       auto load = [&](const CUtensorMap* tm, int kb) {
@@ -191,11 +193,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx(&bar->slot_full[s], L::kSlotBytes);
         tma_load_4d(dst, tm, &bar->slot_full[s], 0, h, kb * BK, b);
         tma_load_4d(dst + L::kSlotPanel, tm, &bar->slot_full[s], 64, h, kb * BK, b);
-        armed[s] = ph;
+        armed |= 1u << s;
+        armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
         ++seq;
         return true;
       };
-      for (int s = 0; s < L::kSlots; ++s) armed[s] = 2;
       ok = load(&tm_k, block_id(0));
       for (int j = 0; ok && j < n; ++j) {
         if (j + 1 < n) ok = load(&tm_k, block_id(j + 1));
@@ -203,8 +205,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // Never leave a copy in flight into shared memory.
       int never = 0;
+#pragma unroll
       for (int s = 0; s < L::kSlots; ++s)
-        if (armed[s] < 2) mbar_wait(&bar->slot_full[s], armed[s], &never, a.err_word);
+        if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
   } else if (warp == kMmaWarp || warp == kPvWarp) {
     // ------------------------------------------------------------ MMA issuers

@@ -99,8 +99,7 @@ __global__ void __launch_bounds__(kMassThreads, 1)
       mbar_arrive_expect_tx(&bar->q_full, kQBytes);
       tma_load_4d(sQ, &tm_q, &bar->q_full, 0, h, qt * kTile, b);
       tma_load_4d(sQ + kPanel, &tm_q, &bar->q_full, 64, h, qt * kTile, b);
-      uint32_t armed[kSlots];
-      for (int s = 0; s < kSlots; ++s) armed[s] = 2;
+      uint32_t armed = 0, armed_phase = 0;  // per slot: a load was issued / its parity
       for (int i = 0; i < steps; ++i) {
         const int s = i % kSlots;
         const uint32_t ph = (i / kSlots) & 1;
@@ -110,12 +109,14 @@ __global__ void __launch_bounds__(kMassThreads, 1)
         mbar_arrive_expect_tx(&bar->slot_full[s], kSlotBytes);
         tma_load_4d(dst, &tm_k, &bar->slot_full[s], 0, h, kt * kTile, b);
         tma_load_4d(dst + kPanel, &tm_k, &bar->slot_full[s], 64, h, kt * kTile, b);
-        armed[s] = ph;
+        armed |= 1u << s;
+        armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
       }
       int never = 0;
       mbar_wait(&bar->q_full, 0, &never, a.err_word);
+#pragma unroll
       for (int s = 0; s < kSlots; ++s)
-        if (armed[s] < 2) mbar_wait(&bar->slot_full[s], armed[s], &never, a.err_word);
+        if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -244,6 +245,286 @@ __global__ void __launch_bounds__(kMassThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// S <= 32 (the sampled route, and the exact mass at 32-token blocks).  Eight
+// softmax warps, two per SM sub-partition: warp w owns rows 32*(w%4).. and
+// column half w/4 of every S tile, keeps its own running (max, sum) over its
+// half-rows in pass 1 and combines it with the other half once, through
+// shared memory, before pass 2.  All score arithmetic is packed (f32x2); the
+// reference's two bf16 roundings (matmul output, then `* score_scale`) run on
+// the FMA pipe by Veltkamp splitting, which leaves the conversion unit, shared
+// with the exponentials, free; a share of the exponentials runs on the FMA pipe
+// too (exp2_poly2).  A query block's S sampled rows are S consecutive lanes,
+// reduced with shuffles.
+//   warp 8 TMA producer, warp 9 TMEM allocator + tcgen05.mma issuer.
+constexpr int kMass2Threads = 320;
+constexpr int kXchgOff = kBiasOff + kMaxBlocks * 4;
+constexpr int kBar2Off = kXchgOff + 2 * 128 * 2 * 4;
+constexpr int kMass2Smem = kBar2Off + 256 + 1024;
+constexpr int kMassEmulated = 2;  // of every 8 column pairs, exponentials on the FMA pipe
+
+// bf16 round-to-nearest-even of two floats without the conversion unit:
+// t = x * (2^16 + 1), hi = t - (t - x) keeps the 8 leading significand bits
+// with ties to even (Veltkamp splitting; exact for |x| < 2^111, far above any
+// score here).  Explicit _rn operations: a fused multiply-add would break it.
+__device__ __forceinline__ float2 round2_bf16(float2 x) {
+  const float2 t = __fmul2_rn(x, make_float2(65537.f, 65537.f));
+  const float2 d = __ffma2_rn(x, make_float2(-1.f, -1.f), t);
+  return __ffma2_rn(d, make_float2(-1.f, -1.f), t);
+}
+
+template <int kEmulate>
+__device__ __forceinline__ float2 exp2_pair(float2 t) {
+  if constexpr (kEmulate) {
+    return exp2_poly2(t);
+  } else {
+    return make_float2(ex2_approx(t.x), ex2_approx(t.y));
+  }
+}
+
+// Log2-domain scores of 64 keys starting at key0 (bias = log(size/S) per key
+// block, keys past n_rows -> -inf), from the raw fp32 accumulators r.
+template <int LOG2S, bool kRound>
+__device__ __forceinline__ void mass_scores(const uint32_t* r, float2* y, int64_t key0,
+                                            int64_t n_rows, const float* sBiasL, float scale) {
+  const float2 sc2 = make_float2(scale, scale);
+  const float2 l2e = make_float2(kLog2eM, kLog2eM);
+  const int64_t kb0 = key0 >> LOG2S;
+#pragma unroll
+  for (int p = 0; p < 32; ++p) {
+    float2 v = make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
+    if constexpr (kRound) {
+      v = round2_bf16(__fmul2_rn(round2_bf16(v), sc2));
+    } else {
+      v = __fmul2_rn(v, sc2);
+    }
+    float2 bl;
+    if constexpr (LOG2S == 0) {
+      bl = make_float2(sBiasL[kb0 + 2 * p], sBiasL[kb0 + 2 * p + 1]);
+    } else {
+      const float bb = sBiasL[kb0 + ((2 * p) >> LOG2S)];
+      bl = make_float2(bb, bb);
+    }
+    y[p] = __ffma2_rn(v, l2e, bl);
+  }
+  if (key0 + 64 > n_rows) {
+#pragma unroll
+    for (int p = 0; p < 32; ++p) {
+      if (key0 + 2 * p >= n_rows) y[p].x = -INFINITY;
+      if (key0 + 2 * p + 1 >= n_rows) y[p].y = -INFINITY;
+    }
+  }
+}
+
+template <int LOG2S, bool kRound>
+__global__ void __launch_bounds__(kMass2Threads, 1)
+    sampled_mass_kernel2(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k, const MassArgs a) {
+  constexpr int S = 1 << LOG2S;
+  constexpr int kHalfBlocks = 64 / S;  // key blocks in a 64-column half tile
+  static_assert(S <= 32, "a query block's rows must fit in one warp");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sRing = smem + kRingOff;
+  float* sBiasL = reinterpret_cast<float*>(smem + kBiasOff);
+  float2* sX = reinterpret_cast<float2*>(smem + kXchgOff);  // [half][row] (max, sum)
+  MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + kBar2Off);
+  volatile int* abort_flag = &bar->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qt = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int n_tiles = static_cast<int>((a.n_rows + kTile - 1) / kTile);
+  const int steps = 2 * n_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->s_free[i], 256);
+    }
+    mbar_init(&bar->drain, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bar->slot_full[s], 1);
+      mbar_init(&bar->slot_empty[s], 1);
+    }
+    bar->abort = prior_timeout(a.err_word) ? 1 : 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (bar->abort) return;  // uniform: set before the barrier, read after it
+  for (int i = threadIdx.x; i < a.q_blocks; i += kMass2Threads)
+    sBiasL[i] = a.block_bias != nullptr ? a.block_bias[i] * kLog2eM : 0.f;
+  if (warp == 9) tmem_alloc(&bar->tmem_base, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      mbar_arrive_expect_tx(&bar->q_full, kQBytes);
+      tma_load_4d(sQ, &tm_q, &bar->q_full, 0, h, qt * kTile, b);
+      tma_load_4d(sQ + kPanel, &tm_q, &bar->q_full, 64, h, qt * kTile, b);
+      uint32_t armed = 0, armed_phase = 0;
+      for (int i = 0; i < steps; ++i) {
+        const int s = i % kSlots;
+        const uint32_t ph = (i / kSlots) & 1;
+        if (!mbar_wait(&bar->slot_empty[s], ph ^ 1, abort_flag, a.err_word)) break;
+        const int kt = i % n_tiles;
+        uint8_t* dst = sRing + s * kSlotBytes;
+        mbar_arrive_expect_tx(&bar->slot_full[s], kSlotBytes);
+        tma_load_4d(dst, &tm_k, &bar->slot_full[s], 0, h, kt * kTile, b);
+        tma_load_4d(dst + kPanel, &tm_k, &bar->slot_full[s], 64, h, kt * kTile, b);
+        armed |= 1u << s;
+        armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
+      }
+      int never = 0;
+      mbar_wait(&bar->q_full, 0, &never, a.err_word);
+#pragma unroll
+      for (int s = 0; s < kSlots; ++s)
+        if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, kTile, false);
+      const uint64_t qdesc = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t kdesc0 = sdesc_sw128(smem_u32(sRing), 16, 1024);
+      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
+      for (int i = 0; ok && i < steps; ++i) {
+        const int s = i % kSlots;
+        ok = mbar_wait(&bar->slot_full[s], (i / kSlots) & 1, abort_flag, a.err_word);
+        if (ok && i >= 2) ok = mbar_wait(&bar->s_free[i & 1], ((i >> 1) - 1) & 1, abort_flag, a.err_word);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t kd = kdesc0 + static_cast<uint64_t>((s * kSlotBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kPanel + (kk & 3) * 32) >> 4);
+          umma_bf16_ss(tmem + (i & 1) * 128, qdesc + off, kd + off, idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar->s_full[i & 1]);
+        umma_commit(&bar->slot_empty[s]);
+      }
+      int never = 0;
+      umma_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0, &never, a.err_word);
+    }
+  } else {
+    const int half = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
+    const int64_t qrow = static_cast<int64_t>(qt) * kTile + row;
+    const int64_t out_rows = (static_cast<int64_t>(b) * a.heads + h) * a.q_blocks;
+    float m2 = -INFINITY, l = 0.f, m_fold = 0.f;
+    for (int i = 0; i < steps; ++i) {
+      if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.err_word)) break;
+      tc_fence_after();
+      uint32_t r[64];
+      tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + half * 64, r);
+      tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + half * 64 + 32, r + 32);
+      tmem_wait_ld();
+      reg_fence<64>(r);
+      tc_fence_before();
+      mbar_arrive(&bar->s_free[i & 1]);
+      const int64_t key0 = static_cast<int64_t>(i % n_tiles) * kTile + half * 64;
+      float2 y[32];
+      mass_scores<LOG2S, kRound>(r, y, key0, a.n_rows, sBiasL, a.scale);
+      if (i < n_tiles) {
+        // Pass 1: running max and sum of this half-row.
+        float m8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) m8[q] = fmaxf(y[q].x, y[q].y);
+#pragma unroll
+        for (int p = 8; p < 32; p += 8) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) m8[q] = fmax3(m8[q], y[p + q].x, y[p + q].y);
+        }
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                               fmaxf(m8[6], m8[7]));
+        const float m_new = fmaxf(m2, mx);
+        // A half-row whose keys so far are all past the sequence (few sampled
+        // rows) keeps (-inf, 0): -inf - -inf would be NaN.
+        if (m_new != -INFINITY) {
+          const float2 nm = make_float2(-m_new, -m_new);
+          float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                           make_float2(0.f, 0.f)};
+#pragma unroll
+          for (int p = 0; p < 32; ++p) {
+            const float2 t = __fadd2_rn(y[p], nm);
+            const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
+            acc[p & 3] = __fadd2_rn(acc[p & 3], e);
+          }
+          const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+          l = l * ex2_approx(m2 - m_new) + (a03.x + a03.y);
+          m2 = m_new;
+        }
+        if (i == n_tiles - 1) {
+          // Combine with the other half-row: both warps of these rows meet at
+          // named barrier 1 + wq.
+          sX[half * 128 + row] = make_float2(m2, l);
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + wq) : "memory");
+          const float2 o = sX[(half ^ 1) * 128 + row];
+          const float m_all = fmaxf(m2, o.x);
+          const float l_all = l * ex2_approx(m2 - m_all) + o.y * ex2_approx(o.x - m_all);
+          // 2^(y - m_fold) = 2^(y - m_all) / l_all
+          m_fold = m_all + __log2f(l_all);
+        }
+      } else {
+        // Pass 2: normalised probabilities summed per key block, then over the
+        // S sampled rows of each query block.
+        const float2 nf = make_float2(-m_fold, -m_fold);
+        float g[kHalfBlocks];
+#pragma unroll
+        for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
+#pragma unroll
+        for (int p = 0; p < 32; ++p) {
+          const float2 t = __fadd2_rn(y[p], nf);
+          const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
+          if constexpr (LOG2S == 0) {
+            g[2 * p] += e.x;
+            g[2 * p + 1] += e.y;
+          } else {
+            g[(2 * p) >> LOG2S] += e.x + e.y;
+          }
+        }
+        if (qrow >= a.n_rows) {
+#pragma unroll
+          for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
+        }
+        if constexpr (S > 1) {
+#pragma unroll
+          for (int gi = 0; gi < kHalfBlocks; ++gi) {
+#pragma unroll
+            for (int off = 1; off < S; off <<= 1) g[gi] += __shfl_xor_sync(0xffffffffu, g[gi], off);
+          }
+        }
+        const int64_t qblock = qrow >> LOG2S;
+        const int64_t kb0 = key0 >> LOG2S;
+        if ((lane & (S - 1)) == 0 && qblock < a.q_blocks) {
+          float* dst = a.mass + (out_rows + qblock) * a.q_blocks;
+#pragma unroll
+          for (int gi = 0; gi < kHalfBlocks; ++gi)
+            if (kb0 + gi < a.q_blocks) dst[kb0 + gi] = g[gi] * a.mass_scale;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 template <int LOG2S>
 cudaError_t launch_log2s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                          cudaStream_t stream) {
@@ -263,6 +544,32 @@ cudaError_t launch_log2s(const CUtensorMap& tq, const CUtensorMap& tk, const Mas
   return cudaGetLastError();
 }
 
+template <int LOG2S, bool kRound>
+cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
+                            cudaStream_t stream) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    e = cudaFuncSetAttribute(sampled_mass_kernel2<LOG2S, kRound>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMass2Smem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const dim3 grid(static_cast<unsigned>((a.n_rows + kTile - 1) / kTile),
+                  static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
+  sampled_mass_kernel2<LOG2S, kRound><<<grid, kMass2Threads, kMass2Smem, stream>>>(tq, tk, a);
+  return cudaGetLastError();
+}
+
+template <int LOG2S>
+cudaError_t launch_small_s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
+                           cudaStream_t stream) {
+  return a.round_bf16 ? launch_log2s_v2<LOG2S, true>(tq, tk, a, stream)
+                      : launch_log2s_v2<LOG2S, false>(tq, tk, a, stream);
+}
+
 }  // namespace
 
 cudaError_t launch_sampled_mass(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
@@ -270,12 +577,12 @@ cudaError_t launch_sampled_mass(const CUtensorMap& tq, const CUtensorMap& tk, co
   if (a.batch == 0 || a.heads == 0 || a.n_rows == 0) return cudaSuccess;
   if (a.q_blocks > kMaxBlocks) return cudaErrorInvalidValue;
   switch (a.samples) {
-    case 1: return launch_log2s<0>(tq, tk, a, stream);
-    case 2: return launch_log2s<1>(tq, tk, a, stream);
-    case 4: return launch_log2s<2>(tq, tk, a, stream);
-    case 8: return launch_log2s<3>(tq, tk, a, stream);
-    case 16: return launch_log2s<4>(tq, tk, a, stream);
-    case 32: return launch_log2s<5>(tq, tk, a, stream);
+    case 1: return launch_small_s<0>(tq, tk, a, stream);
+    case 2: return launch_small_s<1>(tq, tk, a, stream);
+    case 4: return launch_small_s<2>(tq, tk, a, stream);
+    case 8: return launch_small_s<3>(tq, tk, a, stream);
+    case 16: return launch_small_s<4>(tq, tk, a, stream);
+    case 32: return launch_small_s<5>(tq, tk, a, stream);
     case 64: return launch_log2s<6>(tq, tk, a, stream);
     case 128: return launch_log2s<7>(tq, tk, a, stream);
     default: return cudaErrorInvalidValue;
