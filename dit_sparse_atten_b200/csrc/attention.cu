@@ -11,30 +11,32 @@
 // blocks of BK = 128 (or 64) tokens.
 //   warp 8      TMA producer: K/V tiles by routed block id into a ring of
 //               shared-memory slots (consumption order K0, K1, V0, K2, V1, ...)
-//   warp 9      TMEM allocator; one thread issues S_j = Q K_j^T
-//   warp 10     one thread issues O += P_j V_j
-//               Both MMAs take A (Q, P) from tensor memory and B (K, V) from
-//               shared memory.  Two issuing threads keep the tensor pipe fed
-//               while either waits on a barrier (the pipe queues only about
-//               one 128x128x16 MMA ahead); descriptors are precomputed so
-//               consecutive MMAs issue back to back.
-//   warps 0-7   softmax.  Warp w owns TMEM lanes 32*(w%4).. (query rows) and
-//               column half w/4 of Q, of every S tile and of O.  They first
-//               copy their Q rows from global memory into TMEM.  The two warps
-//               of a row exchange half-row maxima through shared memory (named
-//               barrier 1 + w%4, 64 threads); each keeps its own partial row
-//               sum.  Scores are handled in the log2 domain with a running
+//   warp 9      TMEM allocator; one thread TMA-loads Q into shared memory and
+//               issues S_j = Q K_j^T (A and B from shared memory)
+//   warp 10     one thread issues O += P_j V_j (A = P from tensor memory)
+//               Two issuing threads keep the tensor pipe fed while either
+//               waits on a barrier (the pipe queues only about one
+//               128x128x16 MMA ahead).
+//   warps 0-7   softmax, two groups of four warps taking alternate key blocks
+//               (group g = w/4 handles blocks j with j % 2 == g), so a group
+//               has two block periods for its softmax.  Warp w owns TMEM lanes
+//               32*(w%4).. (query rows), one full row per thread, read from
+//               TMEM twice (row max, then exponentials in 32-column chunks).
+//               Scores are handled in the log2 domain with a running
 //               stabiliser that only moves when the max grows by more than 2^8
-//               (then O is rescaled in TMEM).  P_j (bf16) is written into the
-//               first BK/2 columns of S_j's own TMEM buffer; the epilogue
-//               normalises O and stores it.
-// TMEM columns: S (and P) buffers at [0,128) and [128,256), O at [256,384),
-// Q at [384,448).  Shared memory holds only K/V tiles, so per key block the
-// tensor pipe reads 64 KB from it and TMA writes 64 KB.
-// Ordering: S_{j+2} overwrites P_j, so the S issuer waits for PV_j (o_done);
-// the softmax never waits for the previous PV unless it rescales O.  p_full
-// and o_done alternate between two barriers by block parity so no waiter can
-// fall two phases behind.
+//               (then O is rescaled in TMEM); it passes from group to group
+//               through shared memory (m_full barriers), each group keeps its
+//               own row sum and the epilogue combines the two.  P_j (bf16) is
+//               written into the first BK/2 columns of S_j's own TMEM buffer;
+//               the epilogue normalises O and stores it (group g writes
+//               features 64 g .. 64 g + 63).
+// TMEM columns: three S (and P) buffers at [0,128), [128,256), [256,384), O at
+// [384,512).  Shared memory: Q (32 KB) and the K/V ring.
+// Ordering: S_{j+3} overwrites P_j, so the S issuer waits for PV_j (o_done);
+// with three buffers a group's next S never waits for its own softmax.  The
+// softmax waits for the previous PV only when it rescales O.  Barriers of a
+// buffer complete once per three blocks, and no waiter can fall two phases
+// behind (each next phase needs the waiter's own progress).
 // Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
 // kErrWaitTimeout in the caller's error word, drains its in-flight copies and
 // MMAs, frees TMEM and exits.
@@ -49,8 +51,8 @@ constexpr int kMmaWarp = 9;      // S issuer, TMEM owner
 constexpr int kPvWarp = 10;      // PV issuer
 constexpr int kAttnThreads = 352;
 constexpr int kHeadDim = 128;
-constexpr uint32_t kTmemO = 256;
-constexpr uint32_t kTmemQ = 384;
+constexpr int kSBuffers = 3;            // S/P buffers in TMEM
+constexpr uint32_t kTmemO = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -65,23 +67,25 @@ template <int BK>
 struct AttnLayout {
   static constexpr int kSlotPanel = BK * 128;            // one 64-column panel of K or V
   static constexpr int kSlotBytes = 2 * kSlotPanel;
-  static constexpr int kSlots = BK == 128 ? 7 : 8;
-  static constexpr int kRingOff = 0;
-  static constexpr int kXOff = kRingOff + kSlots * kSlotBytes;   // half-row exchange
-  static constexpr int kXBytes = 2 * 2 * 128 * 4;                // [parity][half][row] floats
+  static constexpr int kSlots = BK == 128 ? 6 : 12;
+  static constexpr int kQOff = 0;                                // Q tile, 128 rows x 256 B
+  static constexpr int kRingOff = kQOff + 128 * 256;
+  static constexpr int kXOff = kRingOff + kSlots * kSlotBytes;   // stabiliser hand-over
+  static constexpr int kXBytes = 2 * 2 * 128 * 4;                // [2][2][row] floats
   static constexpr int kBarOff = kXOff + kXBytes;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 320;
   static constexpr int kUsed = kBarOff + kBarBytes;
 };
 
 struct AttnBarriers {
   uint64_t q_full;
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t o_done[2];
+  uint64_t s_full[kSBuffers];
+  uint64_t p_full[kSBuffers];
+  uint64_t m_full[2];
+  uint64_t o_done[kSBuffers];
   uint64_t drain[2];
-  uint64_t slot_full[8];
-  uint64_t slot_empty[8];
+  uint64_t slot_full[12];
+  uint64_t slot_empty[12];
   uint32_t tmem_base;
   int abort;
 };
@@ -99,26 +103,109 @@ __device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
   return __byte_perm(a, b, 0x7632);
 }
 
-template <int N>
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) {
-  if constexpr (N == 32) {
-    tmem_st_32x32b_x32(taddr, r);
-  } else {
-    static_assert(N == 16, "16 or 32 columns");
-    tmem_st_32x32b_x16(taddr, r);
+// The softmax reads a BK-column S row from TMEM in 32-column chunks, twice: a
+// first pass for the row max (all chunks loaded, one wait), a second for the
+// exponentials (two chunk buffers alternate, so the next chunk's load overlaps
+// the current chunk's arithmetic and the row never sits in registers whole).
+
+// Columns of a chunk at or past `valid` (keys beyond the sequence) -> -inf.
+__device__ __forceinline__ void mask_chunk(uint32_t* r, int c0, int64_t valid) {
+#pragma unroll
+  for (int x = 0; x < 32; ++x)
+    if (c0 + x >= valid) r[x] = __float_as_uint(-INFINITY);
+}
+
+// Running row max of a chunk in 8 independent three-input chains.
+__device__ __forceinline__ void max_chunk(float* m8, const uint32_t* r) {
+#pragma unroll
+  for (int x = 0; x < 32; x += 16) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      m8[q] = fmax3(m8[q], __uint_as_float(r[x + 2 * q]), __uint_as_float(r[x + 2 * q + 1]));
   }
+}
+
+// p = 2^(s*c - m) for one chunk: packed FMA for the argument, MUFU for most
+// pairs and the FMA-pipe polynomial for kEmulated of every 8 pairs; the bf16
+// pairs go to 16 TMEM columns at pdst; the sums into four packed accumulators.
+template <int kEmulated>
+__device__ __forceinline__ void exp_chunk(const uint32_t* r, float2 c2, float2 neg_m,
+                                          float2* acc, uint32_t pdst) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int x = 0; x < 32; x += 2) {
+    const float2 t =
+        __ffma2_rn(make_float2(__uint_as_float(r[x]), __uint_as_float(r[x + 1])), c2, neg_m);
+    float2 p;
+    if (((x >> 1) & 7) >= 8 - kEmulated) {
+      p = exp2_poly2(t);
+    } else {
+      p.x = ex2_approx(t.x);
+      p.y = ex2_approx(t.y);
+    }
+    acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], p);
+    pk[x >> 1] = pack_bf16x2_alu(p.x, p.y);
+  }
+  tmem_st_32x32b_x16(pdst, pk);
+}
+
+// First pass: the row max (raw scores) of the BK-column S row at sbuf.
+template <int BK>
+__device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t valid) {
+  constexpr int kChunks = BK / 32;
+  uint32_t r[kChunks][32];
+  float m8[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) m8[q] = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) tmem_ld_32x32b_x32(sbuf + k * 32, r[k]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    reg_fence<32>(r[k]);
+    if (partial) mask_chunk(r[k], k * 32, valid);
+    max_chunk(m8, r[k]);
+  }
+  return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+}
+
+// Second pass: P (bf16) of the row into the first BK/2 columns of its own S
+// buffer (chunk k's P goes to columns [16k, 16k + 16), which only chunks
+// already read hold).  Returns the row's partial sums.
+template <int BK, int kEmulated>
+__device__ __forceinline__ float2 row_exp(uint32_t sbuf, bool partial, int64_t valid, float2 c2,
+                                          float2 neg_m) {
+  constexpr int kChunks = BK / 32;
+  uint32_t r[2][32];
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                   make_float2(0.f, 0.f)};
+  tmem_ld_32x32b_x32(sbuf, r[0]);
+  tmem_wait_ld();
+  reg_fence<32>(r[0]);
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    if (k + 1 < kChunks) tmem_ld_32x32b_x32(sbuf + (k + 1) * 32, r[(k + 1) & 1]);
+    if (partial) mask_chunk(r[k & 1], k * 32, valid);
+    exp_chunk<kEmulated>(r[k & 1], c2, neg_m, acc, sbuf + k * 16);
+    if (k + 1 < kChunks) {
+      tmem_wait_ld();
+      reg_fence<32>(r[(k + 1) & 1]);
+    }
+  }
+  return __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
 }
 
 template <int BK>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    bsa_attention_kernel(const __grid_constant__ CUtensorMap tm_k,
+    bsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
   using L = AttnLayout<BK>;
-  constexpr int HC = BK / 2;  // S columns per softmax half
   static_assert(sizeof(AttnBarriers) <= L::kBarBytes, "barrier area");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem + L::kQOff;
   uint8_t* sRing = smem + L::kRingOff;
   float* sX = reinterpret_cast<float*>(smem + L::kXOff);
   AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(smem + L::kBarOff);
@@ -138,16 +225,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     n = n < 0 ? 0 : min(n, min(a.route_cols, a.k_blocks));
   }
 
+  if constexpr (BK < 128) {
+    // The S MMA always reads 128 Q rows; rows past a 64-token block are zero
+    // (TMA writes rows [0, BK) of each 64-feature panel).
+    for (int i = threadIdx.x; i < 2 * (128 - BK) * 8; i += kAttnThreads) {
+      const int panel = i / ((128 - BK) * 8);
+      const int chunk = i % ((128 - BK) * 8);
+      reinterpret_cast<uint4*>(sQ + panel * 16384 + BK * 128)[chunk] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
   if (threadIdx.x == 0) {
     uint32_t dyn_bytes;
     asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_bytes));
     const bool fits = (smem - smem_raw) + L::kUsed <= static_cast<int>(dyn_bytes);
-    mbar_init(&bar->q_full, kSoftmaxWarps * 32);
-    mbar_init(&bar->s_full[0], 1);
-    mbar_init(&bar->s_full[1], 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->p_full[i], kSoftmaxWarps * 32);
+    mbar_init(&bar->q_full, 1);
+    for (int i = 0; i < kSBuffers; ++i) {
+      mbar_init(&bar->s_full[i], 1);
+      mbar_init(&bar->p_full[i], kSoftmaxWarps * 16);   // one group per block
       mbar_init(&bar->o_done[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->m_full[i], kSoftmaxWarps * 16);
       mbar_init(&bar->drain[i], 1);
     }
     for (int s = 0; s < L::kSlots; ++s) {
@@ -218,24 +317,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == kMmaWarp && lane == 0 && n > 0) {
       const uint32_t idesc_s = idesc_bf16_f32(128, BK, false);
       const uint64_t kdesc0 = sdesc_sw128(ring_addr, 16, 1024);
+      const uint64_t qdesc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      tma_prefetch_desc(&tm_q);
+      mbar_arrive_expect_tx(&bar->q_full, BK * 256);
+      tma_load_4d(sQ, &tm_q, &bar->q_full, 0, h, qb * BK, b);
+      tma_load_4d(sQ + 16384, &tm_q, &bar->q_full, 64, h, qb * BK, b);
       bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
       for (int j = 0; ok && j < n; ++j) {
         const int sq = seq_k(j);
         const int s = sq % L::kSlots;
         ok = mbar_wait(&bar->slot_full[s], (sq / L::kSlots) & 1, abort_flag, a.err_word);
-        // S_j overwrites P_{j-2} (same TMEM buffer): PV_{j-2} must be done.
-        if (ok && j >= 2)
-          ok = mbar_wait(&bar->o_done[j & 1], ((j - 2) >> 1) & 1, abort_flag, a.err_word);
+        // S_j overwrites P_{j-3} (same TMEM buffer): PV_{j-3} must be done.
+        const int sb = j % kSBuffers;
+        if (ok && j >= kSBuffers)
+          ok = mbar_wait(&bar->o_done[sb], ((j - kSBuffers) / kSBuffers) & 1, abort_flag,
+                         a.err_word);
         if (!ok) break;
         tc_fence_after();
         const uint64_t kd = kdesc0 + static_cast<uint64_t>((s * L::kSlotBytes) >> 4);
-        const uint32_t d = tmem + (j & 1) * 128;
+        const uint32_t d = tmem + sb * 128;
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
           const uint64_t db = kd + static_cast<uint64_t>(((kk >> 2) * L::kSlotPanel + (kk & 3) * 32) >> 4);
-          umma_bf16_ts(d, tmem + kTmemQ + kk * 8, db, idesc_s, kk > 0 ? 1u : 0u);
+          const uint64_t da = qdesc0 + static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          umma_bf16_ss(d, da, db, idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bar->s_full[j & 1]);
+        umma_commit(&bar->s_full[sb]);
         umma_commit(&bar->slot_empty[s]);
       }
       int never = 0;
@@ -249,17 +356,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int sq = seq_v(j);
         const int s = sq % L::kSlots;
         ok = mbar_wait(&bar->slot_full[s], (sq / L::kSlots) & 1, abort_flag, a.err_word);
-        if (ok) ok = mbar_wait(&bar->p_full[j & 1], (j >> 1) & 1, abort_flag, a.err_word);
+        const int sb = j % kSBuffers;
+        if (ok) ok = mbar_wait(&bar->p_full[sb], (j / kSBuffers) & 1, abort_flag, a.err_word);
         if (!ok) break;
         tc_fence_after();
         const uint64_t vd = vdesc0 + static_cast<uint64_t>((s * L::kSlotBytes) >> 4);
-        const uint32_t pa = tmem + (j & 1) * 128;
+        const uint32_t pa = tmem + sb * 128;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           umma_bf16_ts(tmem + kTmemO, pa + kk * 8, vd + static_cast<uint64_t>((kk * 16 * 128) >> 4),
                        idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bar->o_done[j & 1]);
+        umma_commit(&bar->o_done[sb]);
         umma_commit(&bar->slot_empty[s]);
       }
       int never = 0;
@@ -268,178 +376,112 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int half = warp >> 2;                // column half of Q, S and O
+    // Two groups of four warps take alternate key blocks: group g = warp / 4
+    // handles blocks j with j % 2 == g, one full row per thread (warp w owns
+    // TMEM lanes 32*(w%4)..), so each group has two block periods for its
+    // softmax.  The stabiliser moves from group to group through m_buf and the
+    // m_full barriers; each group keeps its own row sum.
+    const int grp = warp >> 2;
     const int wq = warp & 3;                   // TMEM lane quarter
     const int row = wq * 32 + lane;            // query row == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t pair_barrier = 1 + wq;      // the two warps sharing these lanes
+    const uint32_t pair_barrier = 1 + wq;      // the two warps (one per group) of these lanes
     const bool warp_active = (BK == 128) || (wq < 2);
     const int64_t token = static_cast<int64_t>(qb) * BK + row;
     const bool row_valid = warp_active && row < BK && token < a.tokens;
 
-    // Q rows -> TMEM (this half's 64 features = 32 packed columns).  Rows past
-    // the sequence (or past a 64-token block) are zero.
-    {
-      uint32_t qv[32];
-      if (row_valid) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            a.q + b * a.in_stride_b + token * a.in_stride_t + h * a.in_stride_h + half * 64);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint4 v = __ldg(src + i);
-          qv[4 * i + 0] = v.x;
-          qv[4 * i + 1] = v.y;
-          qv[4 * i + 2] = v.z;
-          qv[4 * i + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) qv[i] = 0u;
-      }
-      tmem_st_32x32b_x32(tmem + lane_addr + kTmemQ + half * 32, qv);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bar->q_full);
-    }
-
+    float* m_buf = sX;                  // [parity][row]: stabiliser used at the block
     const float c = a.scale * kLog2e;
-    float m_used = -INFINITY;
-    float l = 0.f;
+    const float2 c2 = make_float2(c, c);
+    float m_mine = -INFINITY;           // stabiliser of this group's latest block
+    float l = 0.f;                      // this group's row sum, relative to m_mine
     bool ok = true;
-    int kb_next = (warp_active && n > 0) ? block_id(0) : 0;
-    for (int j = 0; ok && j < n; ++j) {
-      ok = mbar_wait(&bar->s_full[j & 1], (j >> 1) & 1, abort_flag, a.err_word);
+    int kb_next = (warp_active && grp < n) ? block_id(grp) : 0;
+    for (int j = grp; ok && j < n; j += 2) {
+      const int sb = j % kSBuffers;
+      ok = mbar_wait(&bar->s_full[sb], (j / kSBuffers) & 1, abort_flag, a.err_word);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t sbuf = tmem + lane_addr + (j & 1) * 128;
-      float s[HC];
-      float p_scale = 1.f;
-      bool need = false;
-      if (warp_active) {
-        const int kb = kb_next;
-        if (j + 1 < n) kb_next = block_id(j + 1);  // hide the next id's load latency
-        uint32_t r[HC];
-#pragma unroll
-        for (int cc = 0; cc < HC / 32; ++cc)
-          tmem_ld_32x32b_x32(sbuf + half * HC + cc * 32, r + cc * 32);
-        tmem_wait_ld();
-        reg_fence<HC>(r);
-#pragma unroll
-        for (int x = 0; x < HC; ++x) s[x] = __uint_as_float(r[x]);
-        const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK - half * HC;
-        const bool partial = valid < HC;
-        if (partial) {
-#pragma unroll
-          for (int x = 0; x < HC; ++x)
-            if (x >= valid) s[x] = -INFINITY;
-        }
-        // Half-row max in 8 independent three-input chains, then the pair's max.
-        float m8[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) m8[t] = fmaxf(s[2 * t], s[2 * t + 1]);
-#pragma unroll
-        for (int x = 16; x < HC; x += 16) {
-#pragma unroll
-          for (int t = 0; t < 8; ++t) m8[t] = fmax3(m8[t], s[x + 2 * t], s[x + 2 * t + 1]);
-        }
-        const float mh = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
-                               fmaxf(m8[6], m8[7]));
-        float* xs = sX + (j & 1) * 256;
-        xs[half * 128 + row] = mh;
-        // The barrier also orders this half's S loads before the other half's
-        // P stores into the same TMEM buffer.
-        tc_fence_before();
-        named_bar_sync(pair_barrier, 64);
-        tc_fence_after();
-        const float mrow = fmaxf(mh, xs[(half ^ 1) * 128 + row]) * c;
-        need = mrow > m_used + kRescaleThreshold;
-        const float m_new = need ? mrow : m_used;
-        p_scale = need ? ex2_approx(m_used - m_new) : 1.f;
-        m_used = m_new;
-        l *= p_scale;
-        // p = 2^(s*c - m): packed FMA; MUFU for most columns and the FMA-pipe
-        // polynomial for kEmulatedPairsPer8 of every 8 column pairs of full
-        // blocks; partial sums in 4 independent packed accumulators.
-        const float2 c2 = make_float2(c, c);
-        const float2 neg_m = make_float2(-m_used, -m_used);
-        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                         make_float2(0.f, 0.f)};
-        if (partial) {
-#pragma unroll
-          for (int x = 0; x < HC; x += 2) {
-            const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
-            s[x] = ex2_approx(t.x);
-            s[x + 1] = ex2_approx(t.y);
-            acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], make_float2(s[x], s[x + 1]));
-          }
-        } else {
-#pragma unroll
-          for (int x = 0; x < HC; x += 2) {
-            const float2 t = __ffma2_rn(make_float2(s[x], s[x + 1]), c2, neg_m);
-            float2 p;
-            if (((x >> 1) & 7) >= 8 - kEmulatedPairsPer8) {
-              p = exp2_poly2(t);
-            } else {
-              p.x = ex2_approx(t.x);
-              p.y = ex2_approx(t.y);
-            }
-            s[x] = p.x;
-            s[x + 1] = p.y;
-            acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], p);
-          }
-        }
-        const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-        l += a03.x + a03.y;
+      const uint32_t sbuf = tmem + lane_addr + sb * 128;
+      const int kb = kb_next;
+      if (warp_active && j + 2 < n) kb_next = block_id(j + 2);  // hide the next id's latency
+      const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
+      const bool partial = valid < BK;
+      const float mrow = warp_active ? row_max<BK>(sbuf, partial, valid) * c : -INFINITY;
+      // The previous block's stabiliser (decided by the other group).
+      float m_prev = -INFINITY;
+      if (j > 0) {
+        ok = mbar_wait(&bar->m_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err_word);
+        if (!ok) break;
+        m_prev = m_buf[((j - 1) & 1) * 128 + row];
       }
+      const bool need = mrow > m_prev + kRescaleThreshold;
+      const float m_used = need ? mrow : m_prev;
+      m_buf[(j & 1) * 128 + row] = m_used;
+      mbar_arrive(&bar->m_full[j & 1]);
       if (warp_active) {
-        // Only an O rescale has to wait for PV_{j-1} (O must be stable); with
-        // the 2^8 slack that is rare after the first blocks.
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-          ok = mbar_wait(&bar->o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err_word);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int cc = 0; cc < kHeadDim / 64; ++cc) {
+        l *= ex2_approx(m_mine - m_used);  // m_mine = -inf at this group's first block: l = 0
+        m_mine = m_used;
+        const float2 neg_m = make_float2(-m_used, -m_used);
+        // Partial blocks (masked columns) take every exponential on MUFU.
+        const float2 rs = partial ? row_exp<BK, 0>(sbuf, true, valid, c2, neg_m)
+                                  : row_exp<BK, kEmulatedPairsPer8>(sbuf, false, valid, c2, neg_m);
+        l += rs.x + rs.y;
+      }
+      // O holds the blocks before j relative to m_prev: a moved stabiliser
+      // rescales it once PV_{j-1} is done (rare after the first blocks).
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        ok = mbar_wait(&bar->o_done[(j - 1) % kSBuffers], ((j - 1) / kSBuffers) & 1, abort_flag,
+                       a.err_word);
+        if (!ok) break;
+        tc_fence_after();
+        if (warp_active) {
+          const float p_scale = need ? ex2_approx(m_prev - m_used) : 1.f;
+#pragma unroll 1
+          for (int cc = 0; cc < kHeadDim / 32; ++cc) {
             uint32_t o[32];
-            const uint32_t addr = tmem + lane_addr + kTmemO + half * 64 + cc * 32;
+            const uint32_t addr = tmem + lane_addr + kTmemO + cc * 32;
             tmem_ld_32x32b_x32(addr, o);
             tmem_wait_ld();
             reg_fence<32>(o);
 #pragma unroll
             for (int x = 0; x < 32; ++x) o[x] = __float_as_uint(__uint_as_float(o[x]) * p_scale);
             tmem_st_32x32b_x32(addr, o);
-            tmem_wait_st();
           }
         }
-        // P_j (bf16 pairs) into the first BK/2 columns of S_j's buffer.
-        uint32_t pk[HC / 2];
-#pragma unroll
-        for (int x = 0; x < HC / 2; ++x) pk[x] = pack_bf16x2_alu(s[2 * x], s[2 * x + 1]);
-        tmem_st_cols<HC / 2>(sbuf + half * (HC / 2), pk);
-        tmem_wait_st();
       }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bar->p_full[j & 1]);
+      mbar_arrive(&bar->p_full[sb]);
     }
     // ---------------------------------------------------------- epilogue
+    // Both groups' (stabiliser, sum) meet through shared memory; the final
+    // stabiliser is the larger one (it never decreases along the blocks).
+    // Group g then writes output features [64 g, 64 g + 64).
+    float* xs = sX;  // [group][row] stabilisers, then [group][row] sums
+    named_bar_sync(pair_barrier, 64);    // both groups are past their last m_buf read
+    xs[grp * 128 + row] = m_mine;
+    xs[256 + grp * 128 + row] = l;
+    named_bar_sync(pair_barrier, 64);
+    const float m_o = xs[(grp ^ 1) * 128 + row];
+    const float l_o = xs[256 + (grp ^ 1) * 128 + row];
+    const float m_fin = fmaxf(m_mine, m_o);
+    const float l_row = (m_mine == -INFINITY ? 0.f : l * ex2_approx(m_mine - m_fin)) +
+                        (m_o == -INFINITY ? 0.f : l_o * ex2_approx(m_o - m_fin));
     if (ok && n > 0) {
-      ok = mbar_wait(&bar->o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, abort_flag, a.err_word);
+      ok = mbar_wait(&bar->o_done[(n - 1) % kSBuffers], ((n - 1) / kSBuffers) & 1, abort_flag,
+                     a.err_word);
       tc_fence_after();
     }
     if (warp_active) {
-      // Row sum = both halves' partial sums.
-      float* xs = sX + (n & 1) * 256;
-      xs[half * 128 + row] = l;
-      named_bar_sync(pair_barrier, 64);
-      const float l_row = l + xs[(half ^ 1) * 128 + row];
       __nv_bfloat16* out =
-          a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h + half * 64;
+          a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h + grp * 64;
       const float inv_l = (n > 0 && l_row > 0.f) ? 1.f / l_row : 0.f;
-#pragma unroll
+#pragma unroll 1
       for (int cc = 0; cc < kHeadDim / 64; ++cc) {
         uint32_t o[32];
         if (ok && n > 0) {
-          tmem_ld_32x32b_x32(tmem + lane_addr + kTmemO + half * 64 + cc * 32, o);
+          tmem_ld_32x32b_x32(tmem + lane_addr + kTmemO + grp * 64 + cc * 32, o);
           tmem_wait_ld();
           reg_fence<32>(o);
         } else {
@@ -462,9 +504,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
-      if (row_valid && half == 0 && a.lse != nullptr) {
+      if (row_valid && grp == 0 && a.lse != nullptr) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
-            (n > 0 && l_row > 0.f) ? (m_used + __log2f(l_row)) * kLn2 : -INFINITY;
+            (n > 0 && l_row > 0.f) ? (m_fin + __log2f(l_row)) * kLn2 : -INFINITY;
       }
     }
   }
@@ -477,8 +519,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 template <int BK>
-cudaError_t launch_bk(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a,
-                      cudaStream_t stream) {
+cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                      const AttnArgs& a, cudaStream_t stream) {
   using L = AttnLayout<BK>;
   // The layout needs kUsed bytes from a 1024-byte-aligned base; ask for up to
   // 1 KB of slack within the opt-in limit (the kernel checks and reports).
@@ -500,7 +542,7 @@ cudaError_t launch_bk(const CUtensorMap& tk, const CUtensorMap& tv, const AttnAr
   }
   const dim3 grid(static_cast<unsigned>(a.q_blocks), static_cast<unsigned>(a.heads),
                   static_cast<unsigned>(a.batch));
-  bsa_attention_kernel<BK><<<grid, kAttnThreads, bytes, stream>>>(tk, tv, a);
+  bsa_attention_kernel<BK><<<grid, kAttnThreads, bytes, stream>>>(tq, tk, tv, a);
   return cudaGetLastError();
 }
 
@@ -508,10 +550,9 @@ cudaError_t launch_bk(const CUtensorMap& tk, const CUtensorMap& tv, const AttnAr
 
 cudaError_t launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnArgs& a, cudaStream_t stream) {
-  (void)tq;  // Q rows are read directly into tensor memory
   if (a.batch == 0 || a.heads == 0 || a.q_blocks == 0) return cudaSuccess;
-  if (a.block == 128) return launch_bk<128>(tk, tv, a, stream);
-  if (a.block == 64) return launch_bk<64>(tk, tv, a, stream);
+  if (a.block == 128) return launch_bk<128>(tq, tk, tv, a, stream);
+  if (a.block == 64) return launch_bk<64>(tq, tk, tv, a, stream);
   return cudaErrorInvalidValue;
 }
 
