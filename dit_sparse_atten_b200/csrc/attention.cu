@@ -57,9 +57,11 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Of every 8 column pairs of a full key block, this many take their
-// exponentials on the FMA pipe (exp2_poly2) instead of MUFU.
+// exponentials on the FMA pipe (exp2_poly2) instead of MUFU.  Measured on
+// B200: the softmax is bound by instruction issue, not by MUFU, so the default
+// keeps every exponential on MUFU (one instruction per value).
 #ifndef BSA_EMULATED_PAIRS
-#define BSA_EMULATED_PAIRS 2
+#define BSA_EMULATED_PAIRS 0
 #endif
 constexpr int kEmulatedPairsPer8 = BSA_EMULATED_PAIRS;
 
@@ -94,19 +96,10 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// bf16x2 from two floats, round half up on the magnitude (integer ALU instead
-// of the conversion unit, which the exponentials also use).  Non-negative
-// finite inputs only (probabilities).
-__device__ __forceinline__ uint32_t pack_bf16x2_alu(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo) + 0x8000u;
-  const uint32_t b = __float_as_uint(hi) + 0x8000u;
-  return __byte_perm(a, b, 0x7632);
-}
-
-// The softmax reads a BK-column S row from TMEM in 32-column chunks, twice: a
-// first pass for the row max (all chunks loaded, one wait), a second for the
-// exponentials (two chunk buffers alternate, so the next chunk's load overlaps
-// the current chunk's arithmetic and the row never sits in registers whole).
+// The softmax reads a BK-column S row from TMEM in 32-column chunks: a first
+// pass for the row max (all chunks loaded, one wait), then the exponentials,
+// for which the first chunks are read again (the whole row does not fit the
+// 168-register budget next to the exponential pass's own state).
 
 // Columns of a chunk at or past `valid` (keys beyond the sequence) -> -inf.
 __device__ __forceinline__ void mask_chunk(uint32_t* r, int c0, int64_t valid) {
@@ -125,9 +118,10 @@ __device__ __forceinline__ void max_chunk(float* m8, const uint32_t* r) {
   }
 }
 
-// p = 2^(s*c - m) for one chunk: packed FMA for the argument, MUFU for most
-// pairs and the FMA-pipe polynomial for kEmulated of every 8 pairs; the bf16
-// pairs go to 16 TMEM columns at pdst; the sums into four packed accumulators.
+// p = 2^(s*c - m) for one chunk: packed FMA for the argument, MUFU (or, for
+// kEmulated of every 8 pairs, the FMA-pipe polynomial); the pairs are rounded
+// to bf16 (nearest even, one conversion per pair) into 16 TMEM columns at
+// pdst, and summed in fp32 into four packed accumulators.
 template <int kEmulated>
 __device__ __forceinline__ void exp_chunk(const uint32_t* r, float2 c2, float2 neg_m,
                                           float2* acc, uint32_t pdst) {
@@ -144,54 +138,78 @@ __device__ __forceinline__ void exp_chunk(const uint32_t* r, float2 c2, float2 n
       p.y = ex2_approx(t.y);
     }
     acc[(x >> 1) & 3] = __fadd2_rn(acc[(x >> 1) & 3], p);
-    pk[x >> 1] = pack_bf16x2_alu(p.x, p.y);
+    pk[x >> 1] = pack_bf16x2(p.x, p.y);
   }
   tmem_st_32x32b_x16(pdst, pk);
 }
 
-// First pass: the row max (raw scores) of the BK-column S row at sbuf.
+// Chunks of a row the first pass keeps in registers for the second (the
+// rest are read from TMEM again): as many as the register budget allows.
 template <int BK>
-__device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t valid) {
+constexpr int kKeptChunks = BK == 128 ? 2 : 1;
+
+// First pass: the row max (raw scores) of the BK-column S row at sbuf, all
+// chunks loaded at once; the last kKeptChunks chunks stay in `keep` (masked)
+// for the second pass.
+template <int BK>
+__device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t valid,
+                                         uint32_t (&keep)[kKeptChunks<BK>][32]) {
   constexpr int kChunks = BK / 32;
-  uint32_t r[kChunks][32];
+  constexpr int kFirst = kChunks - kKeptChunks<BK>;
+  uint32_t r[kFirst][32];
   float m8[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) m8[q] = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < kChunks; ++k) tmem_ld_32x32b_x32(sbuf + k * 32, r[k]);
+  for (int k = 0; k < kFirst; ++k) tmem_ld_32x32b_x32(sbuf + k * 32, r[k]);
+#pragma unroll
+  for (int k = 0; k < kKeptChunks<BK>; ++k) tmem_ld_32x32b_x32(sbuf + (kFirst + k) * 32, keep[k]);
   tmem_wait_ld();
 #pragma unroll
-  for (int k = 0; k < kChunks; ++k) {
+  for (int k = 0; k < kFirst; ++k) {
     reg_fence<32>(r[k]);
     if (partial) mask_chunk(r[k], k * 32, valid);
     max_chunk(m8, r[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < kKeptChunks<BK>; ++k) {
+    reg_fence<32>(keep[k]);
+    if (partial) mask_chunk(keep[k], (kFirst + k) * 32, valid);
+    max_chunk(m8, keep[k]);
   }
   return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
 }
 
 // Second pass: P (bf16) of the row into the first BK/2 columns of its own S
 // buffer (chunk k's P goes to columns [16k, 16k + 16), which only chunks
-// already read hold).  Returns the row's partial sums.
+// already read hold).  The first chunks are read from TMEM again (two buffers
+// alternate so a load overlaps the previous chunk's arithmetic); the kept
+// ones come from `keep`, already masked.  Returns the row's partial sums.
 template <int BK, int kEmulated>
 __device__ __forceinline__ float2 row_exp(uint32_t sbuf, bool partial, int64_t valid, float2 c2,
-                                          float2 neg_m) {
+                                          float2 neg_m,
+                                          const uint32_t (&keep)[kKeptChunks<BK>][32]) {
   constexpr int kChunks = BK / 32;
-  uint32_t r[2][32];
+  constexpr int kReload = kChunks - kKeptChunks<BK>;
   float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                    make_float2(0.f, 0.f)};
+  uint32_t r[2][32];
   tmem_ld_32x32b_x32(sbuf, r[0]);
   tmem_wait_ld();
   reg_fence<32>(r[0]);
 #pragma unroll
-  for (int k = 0; k < kChunks; ++k) {
-    if (k + 1 < kChunks) tmem_ld_32x32b_x32(sbuf + (k + 1) * 32, r[(k + 1) & 1]);
+  for (int k = 0; k < kReload; ++k) {
+    if (k + 1 < kReload) tmem_ld_32x32b_x32(sbuf + (k + 1) * 32, r[(k + 1) & 1]);
     if (partial) mask_chunk(r[k & 1], k * 32, valid);
     exp_chunk<kEmulated>(r[k & 1], c2, neg_m, acc, sbuf + k * 16);
-    if (k + 1 < kChunks) {
+    if (k + 1 < kReload) {
       tmem_wait_ld();
       reg_fence<32>(r[(k + 1) & 1]);
     }
   }
+#pragma unroll
+  for (int k = 0; k < kKeptChunks<BK>; ++k)
+    exp_chunk<kEmulated>(keep[k], c2, neg_m, acc, sbuf + (kReload + k) * 16);
   return __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
 }
 
@@ -407,7 +425,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (warp_active && j + 2 < n) kb_next = block_id(j + 2);  // hide the next id's latency
       const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
       const bool partial = valid < BK;
-      const float mrow = warp_active ? row_max<BK>(sbuf, partial, valid) * c : -INFINITY;
+      uint32_t keep[kKeptChunks<BK>][32];
+      const float mrow = warp_active ? row_max<BK>(sbuf, partial, valid, keep) * c : -INFINITY;
       // The previous block's stabiliser (decided by the other group).
       float m_prev = -INFINITY;
       if (j > 0) {
@@ -424,8 +443,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_mine = m_used;
         const float2 neg_m = make_float2(-m_used, -m_used);
         // Partial blocks (masked columns) take every exponential on MUFU.
-        const float2 rs = partial ? row_exp<BK, 0>(sbuf, true, valid, c2, neg_m)
-                                  : row_exp<BK, kEmulatedPairsPer8>(sbuf, false, valid, c2, neg_m);
+        const float2 rs = partial ? row_exp<BK, 0>(sbuf, true, valid, c2, neg_m, keep)
+                                  : row_exp<BK, kEmulatedPairsPer8>(sbuf, false, valid, c2, neg_m, keep);
         l += rs.x + rs.y;
       }
       // O holds the blocks before j relative to m_prev: a moved stabiliser
