@@ -326,10 +326,17 @@ def main(argv=None):
     ms = start.elapsed_time(end) / args.steps
     attn_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_events)
     _native.check_device_errors()
+    rank_ms = None
     if world > 1:
-        t = torch.tensor([ms, attn_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, attn_ms = float(t[0]), float(t[1])
+        # Per-rank step and attention times (max over ranks is the reported
+        # figure; the spread shows load imbalance between head shards).
+        mine = torch.tensor([ms, attn_ms], device=device, dtype=torch.float64)
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        rank_ms = {"step": [round(float(e[0]), 3) for e in every],
+                   "attention": [round(float(e[1]), 3) for e in every]}
+        ms = max(float(e[0]) for e in every)
+        attn_ms = max(float(e[1]) for e in every)
 
     # per-stage breakdown (one extra step, rank-local)
     stages = {}
@@ -386,6 +393,7 @@ def main(argv=None):
         "stages": stages,
         "roofline": roofline,
         "gpu_launches": 3 * args.steps * world,
+        **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
