@@ -39,9 +39,9 @@ UNIT = "TFLOPS"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one attention launch per
 # (branch, head) it processes: ncu capture of the 4-head config-4 case (2 branches,
-# 389.1 MB read + 107.0 MB written) divided by 8; traffic grows with the heads
+# 387.8 MB read + 105.8 MB written) divided by 8; traffic grows with the heads
 # processed, so a launch's traffic is this times its branches x heads.
-ATTENTION_TRAFFIC_PER_BRANCH_HEAD = (389.1e6 + 107.0e6) / 8
+ATTENTION_TRAFFIC_PER_BRANCH_HEAD = (387.8e6 + 105.8e6) / 8
 
 
 def parse_args(argv=None):
