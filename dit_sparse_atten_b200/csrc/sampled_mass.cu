@@ -251,10 +251,11 @@ __global__ void __launch_bounds__(kMassThreads, 1)
 // column half w/4 of every S tile, keeps its own running (max, sum) over its
 // half-rows in pass 1 and combines it with the other half once, through
 // shared memory, before pass 2.  All score arithmetic is packed (f32x2); the
-// reference's two bf16 roundings (matmul output, then `* score_scale`) run on
-// the FMA pipe by Veltkamp splitting, which leaves the conversion unit, shared
-// with the exponentials, free; a share of the exponentials runs on the FMA pipe
-// too (exp2_poly2).  A query block's S sampled rows are S consecutive lanes,
+// reference's two bf16 roundings (matmul output, then `* score_scale`) are
+// split between the conversion unit (the first) and the FMA pipe (the second,
+// by Veltkamp splitting), so that neither pipe carries both next to the
+// exponentials; a share of the exponentials runs on the FMA pipe too
+// (exp2_poly2).  A query block's S sampled rows are S consecutive lanes,
 // reduced with shuffles.
 //   warp 8 TMA producer, warp 9 TMEM allocator + tcgen05.mma issuer.
 constexpr int kMass2Threads = 320;
@@ -271,6 +272,15 @@ __device__ __forceinline__ float2 round2_bf16(float2 x) {
   const float2 t = __fmul2_rn(x, make_float2(65537.f, 65537.f));
   const float2 d = __ffma2_rn(x, make_float2(-1.f, -1.f), t);
   return __ffma2_rn(d, make_float2(-1.f, -1.f), t);
+}
+
+// The same rounding through the conversion unit: one cvt.rn.bf16x2 packs both
+// values, two integer operations unpack them.  The kernel rounds the raw score
+// this way and the scaled score by Veltkamp splitting, which balances the
+// conversion/ALU pipes against the FMA pipe (4.9 -> 4.3 ms on config 4).
+__device__ __forceinline__ float2 round2_bf16_cvt(float2 x) {
+  const uint32_t p = pack_bf16x2(x.x, x.y);
+  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
 }
 
 template <int kEmulate>
@@ -294,7 +304,7 @@ __device__ __forceinline__ void mass_scores(const uint32_t* r, float2* y, int64_
   for (int p = 0; p < 32; ++p) {
     float2 v = make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
     if constexpr (kRound) {
-      v = round2_bf16(__fmul2_rn(round2_bf16(v), sc2));
+      v = round2_bf16(__fmul2_rn(round2_bf16_cvt(v), sc2));
     } else {
       v = __fmul2_rn(v, sc2);
     }
