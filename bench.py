@@ -358,7 +358,8 @@ def main(argv=None):
                   "pack_hbm_gbs": 6 * elem / pack_ms / 1e6,
                   "unpack_hbm_gbs": 2 * elem / unpack_ms / 1e6}
         if not args.no_route_stage:
-            stages.update(route_stage(cfg, qp, kp, local_route, kernels, device, stream))
+            stages.update(route_stage(cfg, qp, kp, local_route, kernels, device, stream,
+                                      layout.neighbors(device)))
 
     peaks, peak_src = load_peaks()
     local_flops = kept_flops(local_route, cfg.tokens, cfg.block, cfg.head_dim)
@@ -410,8 +411,9 @@ def main(argv=None):
     return 0
 
 
-def route_stage(cfg, qp, kp, route, kernels, device, stream):
-    """Route decision on this layer: sampled mass (S=16) + prior + top-mass + sink + CSR."""
+def route_stage(cfg, qp, kp, route, kernels, device, stream, neighbors):
+    """Route decision on this layer: sampled mass (S=16) + prior + top-mass + sink + CSR,
+    and the directional frontier update of the same route (flex.py:517-534)."""
     prev = route
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for _ in range(2):
@@ -424,12 +426,27 @@ def route_stage(cfg, qp, kp, route, kernels, device, stream):
     ev[2].record(stream)
     torch.cuda.synchronize()
     mass_ms, select_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    front = kernels.frontier_mask(prev, neighbors)
+    dev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for i in range(3):
+        if i == 2:
+            dev[0].record(stream)
+        kernels.directional_update(mass, prev, neighbors, keep=cfg.keep, persistence=0.5,
+                                   previous_frontier=front, sink_blocks=cfg.sink_blocks)
+    dev[1].record(stream)
+    torch.cuda.synchronize()
+    directional_ms = dev[0].elapsed_time(dev[1])
     B, H, Qb = mass.shape[0], mass.shape[1], mass.shape[2]
+    # mass 4 + previous 1 + frontier 1 + candidates 3 (clear, scatter, final)
+    # + route/frontier/exploration/dropped/added 5 + CSR ids 4 bytes per cell
+    directional_bytes = B * H * Qb * Qb * 18 + B * H * Qb * 4
     sampled = 2 * B * H * Qb * 16 * cfg.head_dim * 2
     select_bytes = B * H * Qb * Qb * (4 + 1 + 1 + 4) + B * H * Qb * 4
     return {"route_mass_ms": mass_ms, "route_select_ms": select_ms,
             "route_mass_tflops": 2 * 2 * B * H * (Qb * 16) ** 2 * cfg.head_dim / mass_ms / 1e9,
             "route_select_hbm_gbs": select_bytes / select_ms / 1e6,
+            "directional_update_ms": directional_ms,
+            "directional_update_hbm_gbs": directional_bytes / directional_ms / 1e6,
             "route_mass_hbm_gbs": (sampled + B * H * Qb * Qb * 4) / mass_ms / 1e6}
 
 

@@ -183,6 +183,87 @@ int bsa_route_select(const float* mass, const uint8_t* prev, int64_t rows, int32
   return ok();
 }
 
+int bsa_frontier_mask(const uint8_t* route, const int32_t* neighbors, int64_t planes,
+                      int32_t blocks, uint8_t* frontier, int32_t* err_word, void* stream) {
+  if (route == nullptr || neighbors == nullptr || frontier == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "route, neighbors and frontier must not be null");
+  if (planes < 0 || blocks <= 0 || blocks > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "blocks must be in [1, 4096] (got %d)", blocks);
+  if (reinterpret_cast<uintptr_t>(neighbors) % 16 != 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "neighbors must be 16-byte aligned");
+  cudaError_t e = bsa::launch_frontier_mask(route, neighbors, planes, blocks, frontier, err_word,
+                                            static_cast<cudaStream_t>(stream), sm_count());
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_frontier_mask launch");
+  return ok();
+}
+
+int bsa_directional_update(const float* mass, const uint8_t* previous, const int32_t* neighbors,
+                           const uint8_t* previous_frontier, int64_t planes, int32_t blocks,
+                           float persistence, float min_ratio, float candidate_bonus,
+                           float budget_scale, int32_t max_blocks, int32_t explore_count,
+                           int32_t expand, int32_t sink_blocks, int32_t rows_per_group,
+                           uint8_t* route_out, uint8_t* frontier_out, uint8_t* candidates,
+                           uint8_t* exploration, uint8_t* dropped, uint8_t* added,
+                           int32_t* counts, int32_t* indices, uint64_t* kept, int32_t* err_word,
+                           void* stream) {
+  if (mass == nullptr || previous == nullptr || neighbors == nullptr || route_out == nullptr ||
+      candidates == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT,
+                "mass, previous, neighbors, route_out and candidates must not be null");
+  if (planes < 0 || blocks <= 0 || blocks > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "blocks must be in [1, 4096] (got %d)", blocks);
+  if (reinterpret_cast<uintptr_t>(neighbors) % 16 != 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "neighbors must be 16-byte aligned");
+  if (max_blocks < 1 || max_blocks > blocks)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "max_blocks must be in [1, blocks] (got %d)", max_blocks);
+  if (explore_count < 0 || explore_count > blocks)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "explore_count must be in [0, blocks] (got %d)",
+                explore_count);
+  if (!(budget_scale > 0.f))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "budget_scale must be positive");
+  if (kept != nullptr && (rows_per_group <= 0 || (planes * blocks) % rows_per_group != 0))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "rows must be a multiple of rows_per_group");
+  bsa::DirectionalArgs a{};
+  a.mass = mass;
+  a.prev = previous;
+  a.neighbors = neighbors;
+  a.prev_frontier = previous_frontier;
+  a.planes = planes;
+  a.n = blocks;
+  a.persistence = persistence;
+  a.min_ratio = min_ratio;
+  a.candidate_bonus = candidate_bonus;
+  a.budget_scale = budget_scale;
+  a.cap = max_blocks;
+  a.explore_count = explore_count;
+  a.expand = expand;
+  a.sink_blocks = sink_blocks < 0 ? 0 : sink_blocks;
+  a.rows_per_group = rows_per_group > 0 ? rows_per_group : 1;
+  a.candidates = candidates;
+  a.route_out = route_out;
+  a.exploration = exploration;
+  a.dropped = dropped;
+  a.added = added;
+  a.counts = counts;
+  a.indices = indices;
+  a.kept = reinterpret_cast<unsigned long long*>(kept);
+  a.err_word = err_word;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t cells = static_cast<size_t>(planes) * blocks * blocks;
+  cudaError_t e = cudaMemsetAsync(candidates, 0, cells, s);
+  if (e == cudaSuccess && kept != nullptr)
+    e = cudaMemsetAsync(kept, 0, sizeof(uint64_t) * (planes * blocks / a.rows_per_group), s);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_directional_update memset");
+  e = bsa::launch_directional_update(a, s, sm_count());
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_directional_update launch");
+  if (frontier_out != nullptr) {
+    e = bsa::launch_frontier_mask(route_out, neighbors, planes, blocks, frontier_out, err_word, s,
+                                  sm_count());
+    if (e != cudaSuccess) return cuda_fail(e, "bsa_directional_update frontier launch");
+  }
+  return ok();
+}
+
 int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch, int64_t heads,
                      int32_t q_blocks, int32_t samples, int32_t head_dim,
                      const float* block_bias, float scale, int32_t round_bf16, float* mass,

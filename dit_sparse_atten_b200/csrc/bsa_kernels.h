@@ -35,6 +35,39 @@ struct SelectArgs {
 };
 cudaError_t launch_route_select(const SelectArgs& args, cudaStream_t stream);
 
+// ---- (f3) directional frontier update ---------------------------------------
+enum DirectionalExpand : int { kExpandQ = 1, kExpandK = 2, kExpandJoint = 4 };
+
+struct DirectionalArgs {
+  const float* mass;              // [planes, n, n] fp32 block mass
+  const uint8_t* prev;            // [planes, n, n] 0/1 previous route
+  const int32_t* neighbors;       // [n, 4] spatial neighbour block ids, -1 = none
+  const uint8_t* prev_frontier;   // [planes, n, n] 0/1, or nullptr (from prev)
+  int64_t planes;
+  int32_t n;
+  float persistence, min_ratio, candidate_bonus, budget_scale;
+  int32_t cap;                    // max(1, ceil(n * keep))
+  int32_t explore_count;          // max(1, ceil(n * fraction)), 0 = no exploration
+  int32_t expand;                 // DirectionalExpand bits
+  int32_t sink_blocks;
+  int32_t rows_per_group;         // rows that share one kept counter
+  uint8_t* candidates;            // [planes, n, n]: zeroed, scattered, then final
+  uint8_t* route_out;             // [planes, n, n] route after the sink
+  uint8_t* exploration;           // [planes, n, n] or nullptr
+  uint8_t* dropped;               // [planes, n, n] or nullptr (before the sink)
+  uint8_t* added;                 // [planes, n, n] or nullptr (before the sink)
+  int32_t* counts;                // [planes * n] or nullptr
+  int32_t* indices;               // [planes * n, n] or nullptr
+  unsigned long long* kept;       // [planes * n / rows_per_group] or nullptr (accumulated)
+  int* err_word;
+};
+// Candidate scatter, then per-row selection; candidates must be zero on entry.
+cudaError_t launch_directional_update(const DirectionalArgs& args, cudaStream_t stream,
+                                      int num_sms);
+cudaError_t launch_frontier_mask(const uint8_t* route, const int32_t* neighbors, int64_t planes,
+                                 int32_t n, uint8_t* frontier, int* err_word,
+                                 cudaStream_t stream, int num_sms);
+
 // ---- (b) sampled block mass ------------------------------------------------
 struct MassArgs {
   int64_t batch, heads, n_rows;   // rows of the [B, n_rows, H, D] inputs

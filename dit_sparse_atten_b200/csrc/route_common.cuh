@@ -1,0 +1,335 @@
+// Row-selection helpers shared by the route-selection kernels (top-mass
+// selection in route_select.cu, the directional budget update in
+// directional.cu): the reference's PyTorch CPU float32 row sum, a block-wide
+// sort of (value descending, block id ascending), the reference's unstable
+// argsort tie order, and the CSR partition of a selected row.  Every function
+// is called by all kSelThreads threads of the CTA unless it says otherwise.
+#pragma once
+
+#include "bsa_kernels.h"
+
+namespace bsa {
+namespace {
+
+constexpr int kSelThreads = 128;
+constexpr int kMaxCols = 4096;
+
+__device__ __forceinline__ uint32_t float_order_key(float v) {
+  if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal: one key
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ int ceil_log2(int v) {
+  return v <= 1 ? 0 : 32 - __clz(v - 1);
+}
+
+// Cascade over `size` items; item i of this lane is x[index(i)].
+template <typename IndexFn>
+__device__ float cascade_sum(const float* x, int size, IndexFn index) {
+  const int level_power = max(4, ceil_log2(size) / 4);
+  const int level_step = 1 << level_power;
+  const int level_mask = level_step - 1;
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  int i = 0;
+  while (i + level_step <= size) {
+    for (int j = 0; j < level_step; ++j, ++i) acc0 = __fadd_rn(acc0, x[index(i)]);
+    acc1 = __fadd_rn(acc1, acc0);
+    acc0 = 0.f;
+    if ((i & (level_mask << level_power)) != 0) continue;
+    acc2 = __fadd_rn(acc2, acc1);
+    acc1 = 0.f;
+    if ((i & (level_mask << (2 * level_power))) != 0) continue;
+    acc3 = __fadd_rn(acc3, acc2);
+    acc2 = 0.f;
+  }
+  for (; i < size; ++i) acc0 = __fadd_rn(acc0, x[index(i)]);
+  acc0 = __fadd_rn(acc0, acc1);
+  acc0 = __fadd_rn(acc0, acc2);
+  acc0 = __fadd_rn(acc0, acc3);
+  return acc0;
+}
+
+// float32 row sum in the reference's CPU order; executed by one full warp,
+// result valid in every lane.
+__device__ float torch_cpu_row_sum(const float* x, int n) {
+  const int lane = threadIdx.x & 31;
+  float result = 0.f;
+  if (n < 8) {
+    if (lane == 0) {
+      const int size_ilp = n / 4;
+      float p[4];
+      for (int k = 0; k < 4; ++k)
+        p[k] = cascade_sum(x, size_ilp, [k](int i) { return 4 * i + k; });
+      for (int i = size_ilp * 4; i < n; ++i) p[0] = __fadd_rn(p[0], x[i]);
+      for (int k = 1; k < 4; ++k) p[0] = __fadd_rn(p[0], p[k]);
+      result = __fadd_rn(0.f, p[0]);
+    }
+    return __shfl_sync(0xffffffffu, result, 0);
+  }
+  const int vec_size = n / 8;
+  const int size_ilp = vec_size / 4;
+  const int k = lane >> 3;
+  const int v = lane & 7;
+  float acc = cascade_sum(x, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
+  if (k == 0)
+    for (int i = size_ilp * 4; i < vec_size; ++i) acc = __fadd_rn(acc, x[i * 8 + v]);
+  const float a1 = __shfl_sync(0xffffffffu, acc, (v + 8) & 31);
+  const float a2 = __shfl_sync(0xffffffffu, acc, (v + 16) & 31);
+  const float a3 = __shfl_sync(0xffffffffu, acc, (v + 24) & 31);
+  float p = __fadd_rn(__fadd_rn(__fadd_rn(acc, a1), a2), a3);
+  float f = 0.f;
+  if (lane == 0)
+    for (int i = vec_size * 8; i < n; ++i) f = __fadd_rn(f, x[i]);
+  for (int l = 0; l < 8; ++l) {
+    const float pl = __shfl_sync(0xffffffffu, p, l);
+    if (lane == 0) f = __fadd_rn(f, pl);
+  }
+  return __shfl_sync(0xffffffffu, f, 0);
+}
+
+// ---------------------------------------------------------------------------
+// Tie order of the reference's unstable `argsort(descending=True)`.
+// The reference sorts (value, index) pairs with libstdc++'s introsort and a
+// key-only greater-than comparator, so equal values end up in the order that
+// algorithm leaves them.  The count of kept blocks does not depend on it (the
+// sorted value sequence is the same), only which of several equal values
+// straddling the cut are kept; for those rows one thread replays the
+// introsort.  Published algorithm: median-of-three quicksort with unguarded
+// partitions, heapsort below a depth limit of 2*floor(log2 n), then insertion
+// sort with a 16-element threshold.
+// ---------------------------------------------------------------------------
+struct SortPair {
+  float v;
+  int32_t i;
+};
+
+__device__ __forceinline__ bool pair_greater(const SortPair& x, const SortPair& y) {
+  return x.v > y.v;
+}
+
+__device__ __forceinline__ void pair_swap(SortPair* a, int x, int y) {
+  const SortPair t = a[x];
+  a[x] = a[y];
+  a[y] = t;
+}
+
+__device__ void move_median_to_first(SortPair* a, int result, int x, int y, int z) {
+  if (pair_greater(a[x], a[y])) {
+    if (pair_greater(a[y], a[z])) pair_swap(a, result, y);
+    else if (pair_greater(a[x], a[z])) pair_swap(a, result, z);
+    else pair_swap(a, result, x);
+  } else if (pair_greater(a[x], a[z])) {
+    pair_swap(a, result, x);
+  } else if (pair_greater(a[y], a[z])) {
+    pair_swap(a, result, z);
+  } else {
+    pair_swap(a, result, y);
+  }
+}
+
+__device__ int unguarded_partition(SortPair* a, int first, int last, int pivot) {
+  for (;;) {
+    while (pair_greater(a[first], a[pivot])) ++first;
+    --last;
+    while (pair_greater(a[pivot], a[last])) --last;
+    if (!(first < last)) return first;
+    pair_swap(a, first, last);
+    ++first;
+  }
+}
+
+__device__ void adjust_heap(SortPair* a, int first, int hole, int len, SortPair value) {
+  const int top = hole;
+  int second = hole;
+  while (second < (len - 1) / 2) {
+    second = 2 * (second + 1);
+    if (pair_greater(a[first + second], a[first + second - 1])) --second;
+    a[first + hole] = a[first + second];
+    hole = second;
+  }
+  if ((len & 1) == 0 && second == (len - 2) / 2) {
+    second = 2 * (second + 1);
+    a[first + hole] = a[first + second - 1];
+    hole = second - 1;
+  }
+  int parent = (hole - 1) / 2;
+  while (hole > top && pair_greater(a[first + parent], value)) {
+    a[first + hole] = a[first + parent];
+    hole = parent;
+    parent = (hole - 1) / 2;
+  }
+  a[first + hole] = value;
+}
+
+__device__ void heap_sort(SortPair* a, int first, int last) {
+  const int len = last - first;
+  if (len >= 2) {
+    for (int parent = (len - 2) / 2;; --parent) {
+      adjust_heap(a, first, parent, len, a[first + parent]);
+      if (parent == 0) break;
+    }
+  }
+  while (last - first > 1) {
+    --last;
+    const SortPair value = a[last];
+    a[last] = a[first];
+    adjust_heap(a, first, 0, last - first, value);
+  }
+}
+
+__device__ void unguarded_linear_insert(SortPair* a, int last) {
+  const SortPair val = a[last];
+  int next = last - 1;
+  while (pair_greater(val, a[next])) {
+    a[last] = a[next];
+    last = next;
+    --next;
+  }
+  a[last] = val;
+}
+
+__device__ void introsort_desc(SortPair* a, int n) {
+  constexpr int kThreshold = 16;
+  if (n <= 0) return;
+  int st_first[64], st_last[64], st_depth[64];
+  int sp = 0;
+  st_first[0] = 0;
+  st_last[0] = n;
+  st_depth[0] = 2 * (31 - __clz(n));
+  sp = 1;
+  // Disjoint subranges are independent, so a stack replaces the recursion.
+  while (sp > 0) {
+    --sp;
+    const int first = st_first[sp];
+    int last = st_last[sp];
+    int depth = st_depth[sp];
+    while (last - first > kThreshold) {
+      if (depth == 0) {
+        heap_sort(a, first, last);
+        break;
+      }
+      --depth;
+      const int mid = first + (last - first) / 2;
+      move_median_to_first(a, first, first + 1, mid, last - 1);
+      const int cut = unguarded_partition(a, first + 1, last, first);
+      st_first[sp] = cut;
+      st_last[sp] = last;
+      st_depth[sp] = depth;
+      ++sp;
+      last = cut;
+    }
+  }
+  const int head = n > kThreshold ? kThreshold : n;
+  for (int i = 1; i < head; ++i) {
+    if (pair_greater(a[i], a[0])) {
+      const SortPair val = a[i];
+      for (int j = i; j > 0; --j) a[j] = a[j - 1];
+      a[0] = val;
+    } else {
+      unguarded_linear_insert(a, i);
+    }
+  }
+  for (int i = head; i < n; ++i) unguarded_linear_insert(a, i);
+}
+
+// Sort key: value descending, then block id ascending.
+__device__ __forceinline__ uint64_t desc_key(float v, int i) {
+  return (static_cast<uint64_t>(~float_order_key(v)) << 32) | static_cast<uint32_t>(i);
+}
+
+__device__ __forceinline__ int key_id(uint64_t key) { return static_cast<int>(key & 0xffffffffu); }
+
+// keys[0, np) <- sorted desc_key(vals[i], i) for i < n, padding (~0) after;
+// np is the power of two >= n.
+__device__ void sort_row_desc(const float* vals, int n, int np, uint64_t* keys) {
+  const int tid = threadIdx.x;
+  for (int i = tid; i < np; i += kSelThreads) keys[i] = i < n ? desc_key(vals[i], i) : ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= np; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int p = tid; p < (np >> 1); p += kSelThreads) {
+        const int lo = ((p / stride) * stride << 1) + (p % stride);
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const uint64_t x = keys[lo], y = keys[hi];
+        if ((x > y) == ascending) {
+          keys[lo] = y;
+          keys[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// flags[i] = 1 for the first `count` entries of the reference's
+// `vals.argsort(descending=True)`, 0 for the rest.  keys holds the output of
+// sort_row_desc(vals); where equal values straddle the cut one thread replays
+// the reference's introsort (keys is reused as its scratch).
+__device__ void mark_first_desc(const float* vals, int n, int count, uint64_t* keys,
+                                uint8_t* flags) {
+  const int tid = threadIdx.x;
+  const bool tie = count > 0 && count < n &&
+                   vals[key_id(keys[count - 1])] == vals[key_id(keys[count])];
+  if (!tie) {
+    for (int r = tid; r < n; r += kSelThreads) flags[key_id(keys[r])] = r < count ? 1 : 0;
+  } else {
+    SortPair* pairs = reinterpret_cast<SortPair*>(keys);
+    __syncthreads();
+    if (tid == 0) {
+      for (int i = 0; i < n; ++i) pairs[i] = SortPair{vals[i], i};
+      introsort_desc(pairs, n);
+    }
+    __syncthreads();
+    for (int r = tid; r < n; r += kSelThreads) flags[pairs[r].i] = r < count ? 1 : 0;
+  }
+  __syncthreads();
+}
+
+// Stable partition of a row's flags into CSR (selected ids ascending, then
+// the rest); writes any of indices / route_out (at row offset base), the count
+// and the kept counter that are non-null.
+__device__ void write_csr_row(const uint8_t* flags, int n, size_t base, int32_t* indices,
+                              uint8_t* route_out, int32_t* count_out,
+                              unsigned long long* kept_slot) {
+  __shared__ int s_warp_tot[kSelThreads / 32];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int per = (n + kSelThreads - 1) / kSelThreads;
+  const int begin = min(n, tid * per);
+  const int end = min(n, begin + per);
+  int local = 0;
+  for (int i = begin; i < end; ++i) local += flags[i];
+  int incl = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) s_warp_tot[warp] = incl;
+  __syncthreads();
+  int warp_off = 0, total = 0;
+  for (int w = 0; w < kSelThreads / 32; ++w) {
+    if (w < warp) warp_off += s_warp_tot[w];
+    total += s_warp_tot[w];
+  }
+  int sel_before = warp_off + incl - local;
+  for (int i = begin; i < end; ++i) {
+    const int f = flags[i];
+    if (indices != nullptr) {
+      const int pos = f ? sel_before : total + (i - sel_before);
+      indices[base + pos] = i;
+    }
+    if (route_out != nullptr) route_out[base + i] = static_cast<uint8_t>(f);
+    sel_before += f;
+  }
+  if (tid == 0) {
+    if (count_out != nullptr) *count_out = total;
+    if (kept_slot != nullptr) atomicAdd(kept_slot, static_cast<unsigned long long>(total));
+  }
+}
+
+}  // namespace
+}  // namespace bsa

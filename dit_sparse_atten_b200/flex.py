@@ -11,11 +11,8 @@ at the final step; ``flex.py:652-850``), and the same module-level helpers
 ``_dense_bootstrap``).  What changes is underneath: FlexAttention, the Triton
 kernels and the PyTorch route arithmetic are replaced by the sm_100a kernels
 (block-sparse attention, sampled/exact block mass, fused prior + top-mass +
-sink + CSR selection, row gather).  The sparse path needs CUDA bf16 tensors
-with head_dim 128 and raises otherwise.
-
-Not built (they raise ``NotImplementedError``): the directional frontier update
-(``directional_update=True``, reference ``routing.py:92-168``).
+sink + CSR selection, directional frontier update, row gather).  The sparse
+path needs CUDA bf16 tensors with head_dim 128 and raises otherwise.
 """
 
 from __future__ import annotations
@@ -190,8 +187,6 @@ class FlexReuseBackend:
             raise ValueError("route_exploration_fraction must be in [0, 1]")
         if c.directional_update and not c.spatial_reorder:
             raise ValueError("directional_update requires spatial_reorder")
-        if c.directional_update:
-            raise NotImplementedError("the directional frontier update is not part of this build")
         self._routing_context = routing_context
         self.process_group = process_group
         self.dense = DenseBackend()
@@ -287,6 +282,24 @@ class FlexReuseBackend:
         mass = _sampled_block_mass(q, k, c.block_size, samples=c.route_samples,
                                    scale=softmax_scale, query_block_chunk=c.sample_query_block_chunk)
         previous = state.get("route")
+        layout = state.get("layout")
+        if c.directional_update and previous is not None and layout is not None:
+            # flex.py:517-534 + the sink of :550-566, in one call
+            r = kernels.directional_update(
+                mass, previous, layout.neighbors(mass.device), keep=c.keep,
+                persistence=c.route_persistence, min_ratio=c.direction_min_ratio,
+                candidate_bonus=c.direction_candidate_bonus, budget_scale=c.route_budget_scale,
+                exploration_fraction=c.route_exploration_fraction,
+                expand_q=c.direction_expand_q, expand_k=c.direction_expand_k,
+                expand_joint=c.direction_expand_joint,
+                previous_frontier=state.get("frontier"), sink_blocks=self._sink_blocks(state))
+            return {
+                "route": r.route,
+                "frontier": r.frontier,
+                "kept": r.kept,
+                "block_mask": BlockRoute(r.counts.unsqueeze(0), r.indices.unsqueeze(0),
+                                         q.shape[1], c.block_size),
+            }
         result = kernels.route_select(
             mass, prev=previous if c.route_persistence else None,
             persistence=c.route_persistence, target=c.mass_target, keep=c.keep,

@@ -216,6 +216,106 @@ def pack_boolean_rows(route: torch.Tensor):
 
 
 # ----------------------------------------------------------------------------
+# (f3) directional frontier update
+# ----------------------------------------------------------------------------
+
+def _square_planes(t: torch.Tensor, name: str) -> tuple[int, int]:
+    if t.dim() < 2 or t.shape[-1] != t.shape[-2]:
+        raise ValueError(f"{name} must be [..., blocks, blocks]")
+    blocks = t.shape[-1]
+    return (t.numel() // (blocks * blocks) if blocks else 0), blocks
+
+
+def _neighbors_i32(neighbors: torch.Tensor, blocks: int, device) -> torch.Tensor:
+    if tuple(neighbors.shape) != (blocks, 4):
+        raise ValueError("neighbors must have shape [blocks, 4]")
+    return neighbors.to(device=device, dtype=torch.int32).contiguous()
+
+
+def frontier_mask(route: torch.Tensor, neighbors: torch.Tensor) -> torch.Tensor:
+    """Bool frontier of a route ``[..., Kb, Kb]`` (``routing.py:10-43``):
+    selected cells with an unselected valid spatial neighbour along Q or K."""
+    device = _require_cuda(route)
+    planes, blocks = _square_planes(route, "route")
+    nb = _neighbors_i32(neighbors, blocks, device)
+    r = route.to(torch.uint8).contiguous()
+    out = torch.empty(route.shape, dtype=torch.uint8, device=device)
+    if planes:
+        _native.call("bsa_frontier_mask", r.data_ptr(), nb.data_ptr(), planes, blocks,
+                     out.data_ptr(), _native.err_word(device).data_ptr(), _stream(device))
+    return out.bool()
+
+
+class DirectionalResult(NamedTuple):
+    route: torch.Tensor         # bool [..., Kb, Kb], after the sink
+    frontier: torch.Tensor      # bool, frontier of ``route``
+    candidates: torch.Tensor    # bool, expansion candidates (not in previous)
+    exploration: torch.Tensor   # bool, exploration cells
+    dropped: torch.Tensor       # bool, previous & ~route (before the sink)
+    added: torch.Tensor         # bool, route & ~previous (before the sink)
+    counts: torch.Tensor        # int32 [..., Kb] CSR counts of ``route``
+    indices: torch.Tensor       # int32 [..., Kb, Kb] CSR ids
+    kept: torch.Tensor          # int64 [planes] selected cells per plane
+
+
+EXPAND_Q, EXPAND_K, EXPAND_JOINT = 1, 2, 4
+
+
+def directional_update(mass: torch.Tensor, previous: torch.Tensor, neighbors: torch.Tensor, *,
+                       keep: float, persistence: float = 0.5, min_ratio: float = 0.0,
+                       candidate_bonus: float = 0.0, budget_scale: float = 1.0,
+                       exploration_fraction: float = 0.0, expand_q: bool = True,
+                       expand_k: bool = True, expand_joint: bool = True,
+                       previous_frontier: torch.Tensor | None = None,
+                       sink_blocks: int = 0) -> DirectionalResult:
+    """Directional frontier update of ``previous`` from fp32 ``mass`` (both
+    ``[..., Kb, Kb]``), then the first-frame sink and the CSR.
+
+    Bit-identical to the reference's ``directional_budget_update``
+    (``routing.py:97-168``) followed by ``_add_first_frame_sink``
+    (``flex.py:550-566``); same argument checks and messages.
+    """
+    device = _require_cuda(mass, previous, previous_frontier)
+    if previous.shape != mass.shape:
+        raise ValueError("previous route and mass must have identical shapes")
+    planes, blocks = _square_planes(mass, "mass")
+    if tuple(neighbors.shape) != (blocks, 4):
+        raise ValueError("neighbors must have shape [blocks, 4]")
+    if budget_scale <= 0:
+        raise ValueError("budget_scale must be positive")
+    if not 0 <= exploration_fraction <= 1:
+        raise ValueError("exploration_fraction must be in [0, 1]")
+    if mass.dtype != torch.float32:
+        raise ValueError("mass must be float32")
+    if previous_frontier is not None and previous_frontier.shape != mass.shape:
+        raise ValueError("previous_frontier and mass must have identical shapes")
+    mass = mass.contiguous()
+    prev = previous.to(torch.uint8).contiguous()
+    front = previous_frontier.to(torch.uint8).contiguous() if previous_frontier is not None else None
+    nb = _neighbors_i32(neighbors, blocks, device)
+    explore = max(1, math.ceil(blocks * exploration_fraction)) if exploration_fraction else 0
+    expand = ((EXPAND_Q if expand_q else 0) | (EXPAND_K if expand_k else 0)
+              | (EXPAND_JOINT if expand_joint else 0))
+    masks = torch.empty((6,) + tuple(mass.shape), dtype=torch.uint8, device=device)
+    route, frontier, cand, expl, dropped, added = masks.unbind(0)
+    counts = torch.empty(mass.shape[:-1], dtype=torch.int32, device=device)
+    indices = torch.empty(mass.shape, dtype=torch.int32, device=device)
+    kept = torch.empty(max(1, planes), dtype=torch.int64, device=device)
+    if planes:
+        _native.call("bsa_directional_update", mass.data_ptr(), prev.data_ptr(), nb.data_ptr(),
+                     _native.ptr(front), planes, blocks, float(persistence), float(min_ratio),
+                     float(candidate_bonus), float(budget_scale), keep_cap(blocks, keep), explore,
+                     expand, int(sink_blocks), blocks, route.data_ptr(), frontier.data_ptr(),
+                     cand.data_ptr(), expl.data_ptr(), dropped.data_ptr(), added.data_ptr(),
+                     counts.data_ptr(), indices.data_ptr(), kept.data_ptr(),
+                     _native.err_word(device).data_ptr(), _stream(device))
+    else:
+        kept.zero_()
+    b = masks.bool()
+    return DirectionalResult(b[0], b[1], b[2], b[3], b[4], b[5], counts, indices, kept[:planes])
+
+
+# ----------------------------------------------------------------------------
 # (a) attention
 # ----------------------------------------------------------------------------
 

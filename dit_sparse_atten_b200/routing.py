@@ -1,36 +1,45 @@
-"""Route bookkeeping on the device (``routing.py:10-41`` of the reference).
+"""Frontier-aware route updates on the GPU (``attention_backends/routing.py``
+of the reference, same names, arguments and error messages).
 
-Only ``frontier_mask`` is provided: the non-directional sampled path records it
-per state for ``profile_summary()``.  The directional budget update of the
-reference (``routing.py:92-168``) is not part of this build.
+``frontier_mask`` and ``directional_budget_update`` run as CUDA kernels
+(``csrc/directional.cu``) through the C ABI; they take CUDA tensors and raise
+on anything else.  The results are bit-identical to the reference's PyTorch
+code from the same inputs, including which of several equal scores is kept.
 """
 
 from __future__ import annotations
 
 import torch
 
-
-def _neighbor_values(tensor, neighbors, axis):
-    heads, blocks, _ = tensor.shape
-    values, valid_values = [], []
-    for direction in range(neighbors.shape[1]):
-        target = neighbors[:, direction].long()
-        valid = target >= 0
-        if axis == 1:
-            idx = target.clamp_min(0).view(1, blocks, 1).expand(heads, blocks, blocks)
-            gathered = torch.gather(tensor, 1, idx)
-            valid_mask = valid.view(1, blocks, 1)
-        else:
-            idx = target.clamp_min(0).view(1, 1, blocks).expand(heads, blocks, blocks)
-            gathered = torch.gather(tensor, 2, idx)
-            valid_mask = valid.view(1, 1, blocks)
-        values.append(gathered)
-        valid_values.append(valid_mask.expand_as(tensor))
-    return torch.stack(values, -1), torch.stack(valid_values, -1)
+from . import kernels
 
 
-def frontier_mask(route, neighbors):
-    """Selected route cells adjacent to an unselected spatial cell."""
-    q_sel, q_valid = _neighbor_values(route, neighbors, axis=1)
-    k_sel, k_valid = _neighbor_values(route, neighbors, axis=2)
-    return (route & (q_valid & ~q_sel).any(-1)) | (route & (k_valid & ~k_sel).any(-1))
+def frontier_mask(route: torch.Tensor, neighbors: torch.Tensor) -> torch.Tensor:
+    """Selected route cells adjacent to an unselected spatial cell
+    (``routing.py:37-43``); ``route`` bool ``[H, Qb, Kb]``, ``neighbors``
+    ``[Kb, 4]`` with -1 for a missing neighbour."""
+    return kernels.frontier_mask(route, neighbors)
+
+
+def directional_budget_update(mass, previous, neighbors, *, keep, persistence=0.5,
+                              min_ratio=0.0, candidate_bonus=0.0, budget_scale=1.0,
+                              exploration_fraction=0.0, expand_q=True, expand_k=True,
+                              expand_joint=True, previous_frontier=None):
+    """Expand only route frontiers, then prune back to a per-row budget
+    (``routing.py:97-168``).  Returns the reference's dict: ``route``,
+    ``frontier``, ``candidates``, ``exploration``, ``dropped``, ``added``."""
+    if previous.shape != mass.shape:
+        raise ValueError("previous route and mass must have identical shapes")
+    if tuple(neighbors.shape) != (mass.shape[-1], 4):
+        raise ValueError("neighbors must have shape [blocks, 4]")
+    if budget_scale <= 0:
+        raise ValueError("budget_scale must be positive")
+    if not 0 <= exploration_fraction <= 1:
+        raise ValueError("exploration_fraction must be in [0, 1]")
+    r = kernels.directional_update(
+        mass, previous, neighbors, keep=keep, persistence=persistence, min_ratio=min_ratio,
+        candidate_bonus=candidate_bonus, budget_scale=budget_scale,
+        exploration_fraction=exploration_fraction, expand_q=expand_q, expand_k=expand_k,
+        expand_joint=expand_joint, previous_frontier=previous_frontier)
+    return {"route": r.route, "frontier": r.frontier, "candidates": r.candidates,
+            "exploration": r.exploration, "dropped": r.dropped, "added": r.added}

@@ -97,6 +97,59 @@ BSA_API int bsa_route_select(const float* mass, const uint8_t* prev, int64_t row
                      int32_t* counts, int32_t* indices, uint64_t* kept, void* stream);
 
 /*
+ * (f3) Frontier of a route: frontier[p, q, k] = route[p, q, k] and some valid
+ * neighbour t of q has route[p, t, k] == 0, or some valid neighbour t of k has
+ * route[p, q, t] == 0.  route / frontier: uint8 0/1 [planes, blocks, blocks]
+ * (a plane is one batch x head route); neighbors: int32 [blocks, 4], 16-byte
+ * aligned, -1 = no neighbour (the spatial layout's block neighbours).  Ids
+ * outside [-1, blocks) set BSA_DEVICE_BAD_ROUTE in err_word (may be NULL)
+ * and count as "no neighbour".  blocks <= 4096.
+ * Replaces: attention_backends/routing.py:10-43 (frontier_mask).
+ */
+BSA_API int bsa_frontier_mask(const uint8_t* route, const int32_t* neighbors, int64_t planes,
+                              int32_t blocks, uint8_t* frontier, int32_t* err_word, void* stream);
+
+/*
+ * (f3) Directional frontier update of a route (the directional branch of the
+ * sampled route update), per plane [blocks, blocks]:
+ *   1. for every cell of previous_frontier (NULL: the frontier of previous),
+ *      the unselected neighbour with the highest mass along Q and along K
+ *      (first of equal maxima), eligible when finite and >= mass * min_ratio;
+ *      candidates at (best q, k) [expand bit 1], (q, best k) [bit 2] and
+ *      (best q, best k) when both are eligible [bit 4], minus previous;
+ *   2. pool = previous | candidates; if explore_count > 0 the explore_count
+ *      highest masses outside the pool join it (exploration);
+ *   3. score = mass + persistence * mean(mass) * previous
+ *                   [+ candidate_bonus * mean(mass) * candidates];
+ *   4. keep the first clamp(ceil(#previous * budget_scale), 1, max_blocks),
+ *      at most #pool and at least 1, pool cells of the score sorted
+ *      descending (the reference's argsort tie order);
+ *   5. dropped = previous & ~route, added = route & ~previous;
+ *   6. force columns [0, sink_blocks) on; write route_out, the CSR (counts,
+ *      indices as bsa_route_select) and kept per group of rows_per_group rows;
+ *   7. frontier_out = frontier of route_out (as bsa_frontier_mask).
+ * The caller computes max_blocks = max(1, ceil(blocks * keep)) and
+ * explore_count = max(1, ceil(blocks * exploration_fraction)) (0 for none).
+ * mass fp32 and all masks uint8 [planes, blocks, blocks]; candidates is
+ * required (scratch and output); exploration / dropped / added / frontier_out /
+ * counts / indices / kept may be NULL.  kept is overwritten.  Float sums follow
+ * the reference's PyTorch CPU order: the route is bit-identical to the
+ * reference's from the same inputs.
+ * Replaces: attention_backends/routing.py:97-168 (directional_budget_update),
+ *           attention_backends/flex.py:517-534 and :550-566 (caller and sink).
+ */
+BSA_API int bsa_directional_update(const float* mass, const uint8_t* previous,
+                                   const int32_t* neighbors, const uint8_t* previous_frontier,
+                                   int64_t planes, int32_t blocks, float persistence,
+                                   float min_ratio, float candidate_bonus, float budget_scale,
+                                   int32_t max_blocks, int32_t explore_count, int32_t expand,
+                                   int32_t sink_blocks, int32_t rows_per_group,
+                                   uint8_t* route_out, uint8_t* frontier_out, uint8_t* candidates,
+                                   uint8_t* exploration, uint8_t* dropped, uint8_t* added,
+                                   int32_t* counts, int32_t* indices, uint64_t* kept,
+                                   int32_t* err_word, void* stream);
+
+/*
  * (b) Sampled block mass.  sampled_q / sampled_k: bf16 [batch, q_blocks * samples,
  * heads, head_dim] contiguous (rows gathered with bsa_reorder_rows through the
  * sample token ids of flex.py:222-231).  block_bias: fp32 [q_blocks], the

@@ -240,3 +240,126 @@ def sampled_route(mass, previous, persistence, target, keep, grid=None, block=12
     if first_frame_sink and grid is not None:
         route = add_first_frame_sink(route, grid, block)
     return route
+
+
+# ----------------------------------------------------------------------------
+# (f3) directional frontier update -- routing.py:10-168
+# Arrays are [..., Q, K] with Q == K (one plane per head); neighbours [K, 4]
+# int, -1 where a block has no spatial neighbour in that direction.
+# ----------------------------------------------------------------------------
+
+def frontier_mask(route, neighbors):
+    """Selected cells with an unselected valid neighbour along Q or K
+    (``routing.py:10-43``)."""
+    route = np.asarray(route, bool)
+    nb = np.asarray(neighbors, np.int64)
+    valid = nb >= 0
+    safe = np.maximum(nb, 0)
+    q_sel = route[..., safe, :]                                # [..., Q, 4, K]
+    open_q = (valid[:, :, None] & ~q_sel).any(-2)
+    k_sel = route[..., :, safe]                                # [..., Q, K, 4]
+    open_k = (valid & ~k_sel).any(-1)
+    return route & (open_q | open_k)
+
+
+def _best_targets(mass, route, neighbors, frontier, axis, min_ratio):
+    """Per frontier cell, the best unselected neighbour along ``axis`` (1 = Q,
+    2 = K) and whether it is eligible (``routing.py:55-84``).  The first of
+    equal maxima wins, as ``Tensor.max(-1)``."""
+    nb = np.asarray(neighbors, np.int64)
+    valid = nb >= 0
+    safe = np.maximum(nb, 0)
+    if axis == 1:
+        values = np.moveaxis(mass[..., safe, :], -2, -1)       # [..., Q, K, 4]
+        sel = np.moveaxis(route[..., safe, :], -2, -1)
+        ok = valid[:, None, :]
+        targets = np.broadcast_to(safe[:, None, :], values.shape)
+    else:
+        values = mass[..., :, safe]
+        sel = route[..., :, safe]
+        ok = valid[None, :, :]
+        targets = np.broadcast_to(safe[None, :, :], values.shape)
+    values = np.where(ok & ~sel, values, np.float32(-np.inf)).astype(np.float32)
+    direction = values.argmax(-1)
+    best = np.take_along_axis(values, direction[..., None], -1)[..., 0]
+    target = np.take_along_axis(targets, direction[..., None], -1)[..., 0]
+    eligible = frontier & np.isfinite(best) & (best >= order.mul_scalar(mass, min_ratio))
+    return target, eligible
+
+
+def _rank_below(values, counts):
+    """``ranks(values.argsort(-1, descending=True)) < counts`` with the
+    reference's tie order (``routing.py:87-94``, ``:145-148``)."""
+    idx = selection_order(values)
+    ranks = np.empty_like(idx)
+    np.put_along_axis(ranks, idx, np.broadcast_to(np.arange(values.shape[-1]), idx.shape), -1)
+    return ranks < np.asarray(counts)[..., None]
+
+
+def directional_budget_update(mass, previous, neighbors, *, keep, persistence=0.5,
+                              min_ratio=0.0, candidate_bonus=0.0, budget_scale=1.0,
+                              exploration_fraction=0.0, expand_q=True, expand_k=True,
+                              expand_joint=True, previous_frontier=None):
+    """``directional_budget_update`` (``routing.py:97-168``): expand the
+    previous route's frontier by one best neighbour per cell along Q, K and
+    both, optionally add the best-mass cells outside the pool, then keep a
+    per-row budget of the highest prior scores inside the pool."""
+    mass = np.asarray(mass, np.float32)
+    prev = np.asarray(previous, bool)
+    blocks = mass.shape[-1]
+    front = (np.asarray(previous_frontier, bool) if previous_frontier is not None
+             else frontier_mask(prev, neighbors))
+    tq, eq = _best_targets(mass, prev, neighbors, front, 1, min_ratio)
+    tk, ek = _best_targets(mass, prev, neighbors, front, 2, min_ratio)
+    lead = np.indices(mass.shape)
+    planes = tuple(lead[:-2])
+    q_idx, k_idx = lead[-2], lead[-1]
+    cand = np.zeros(mass.shape, bool)
+    if expand_q:
+        cand[tuple(p[eq] for p in planes) + (tq[eq], k_idx[eq])] = True
+    if expand_k:
+        cand[tuple(p[ek] for p in planes) + (q_idx[ek], tk[ek])] = True
+    if expand_joint:
+        j = eq & ek
+        cand[tuple(p[j] for p in planes) + (tq[j], tk[j])] = True
+    cand &= ~prev
+    pool = prev | cand
+    exploration = np.zeros_like(pool)
+    if exploration_fraction:
+        count = max(1, math.ceil(blocks * exploration_fraction))
+        masked = np.where(pool, np.float32(-np.inf), mass).astype(np.float32)
+        exploration = _rank_below(masked, np.full(mass.shape[:-1], count))
+        pool = pool | exploration
+    row_scale = order.row_mean(mass)[..., None]
+    score = (mass + order.mul_scalar(row_scale, persistence) * prev.astype(np.float32)
+             ).astype(np.float32)
+    if candidate_bonus:
+        score = (score + order.mul_scalar(row_scale, candidate_bonus)
+                 * cand.astype(np.float32)).astype(np.float32)
+    cap = max(1, math.ceil(blocks * keep))
+    counts = np.ceil(prev.sum(-1).astype(np.float32) * np.float32(budget_scale))
+    counts = np.clip(counts.astype(np.int64), 1, cap)
+    counts = np.maximum(np.minimum(counts, pool.sum(-1)), 1)
+    masked = np.where(pool, score, np.float32(-np.inf)).astype(np.float32)
+    route = _rank_below(masked, counts) & pool
+    return {
+        "route": route,
+        "frontier": frontier_mask(route, neighbors),
+        "candidates": cand,
+        "exploration": exploration,
+        "dropped": prev & ~route,
+        "added": route & ~prev,
+    }
+
+
+def directional_route(mass, previous, neighbors, grid=None, block=128, first_frame_sink=True,
+                      **kw):
+    """The directional branch of ``_sampled_route`` (``flex.py:517-534``)
+    followed by ``_add_first_frame_sink`` (``flex.py:550-566``), which also
+    recomputes the frontier of the sunk route."""
+    result = directional_budget_update(mass, previous, neighbors, **kw)
+    if first_frame_sink and grid is not None:
+        result = dict(result)
+        result["route"] = add_first_frame_sink(result["route"], grid, block)
+        result["frontier"] = frontier_mask(result["route"], neighbors)
+    return result

@@ -45,3 +45,26 @@ def unpack_route(bits, cols):
     import numpy as np
 
     return np.unpackbits(bits, axis=-1, count=cols).astype(bool)
+
+
+DIRECTIONAL_KEYS = ("route", "frontier", "candidates", "exploration", "dropped", "added")
+
+
+def directional_case(golden):
+    """Inputs of ``directional.npz``: the config-3 mass of two heads (plain and
+    quantised to multiples of 1/28,800 so that equal scores straddle the
+    budget cut), their previous route, the 720p block neighbours and the
+    option sets, as ``tests/golden/make_golden.py:directional`` made them."""
+    import json
+
+    import numpy as np
+
+    c3 = golden("config3.npz")
+    lay = golden("layouts.npz")
+    g = golden("directional.npz")
+    mass = np.asarray(c3["mass_heads"], np.float32)
+    scale = np.float32(450 * 64.0)
+    quant = (np.round((mass * scale).astype(np.float32)) / scale).astype(np.float32)
+    prev = unpack_route(c3["prev"], 450)[c3["heads"]]
+    options = json.loads(str(g["options"]))
+    return {"plain": mass, "quant": quant}, prev, lay["720p_neighbors"], options, g

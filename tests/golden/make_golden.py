@@ -27,6 +27,11 @@ Fixtures:
                       digests of Q/K, reference mass of two heads, the
                       reference route and counts.
 * ``blob_routes.npz`` config-2 and config-4 routes from the seeded blob scores.
+* ``directional.npz`` ``directional_budget_update`` (``routing.py:97-168``) and
+                      the sunk route / frontier of ``_add_first_frame_sink``
+                      on the config-3 mass of two heads (plain, and quantised
+                      so that equal scores straddle the budget cut), three
+                      option sets each.
 """
 
 from __future__ import annotations
@@ -49,6 +54,7 @@ sys.path.insert(0, os.environ.get("BSA_REFERENCE", "/root/reference"))
 
 from attention_backends import flex as ref_flex  # noqa: E402
 from attention_backends import layout_ops as ref_layout_ops  # noqa: E402
+from attention_backends import routing as ref_routing  # noqa: E402
 from attention_backends import sparse as ref_sparse  # noqa: E402
 from attention_backends import spatial as ref_spatial  # noqa: E402
 
@@ -197,9 +203,53 @@ def blob_routes():
     np.savez_compressed(HERE / "blob_routes.npz", **arrays)
 
 
+DIRECTIONAL_OPTIONS = (
+    {},
+    {"min_ratio": 0.5, "candidate_bonus": 0.25, "budget_scale": 1.1,
+     "exploration_fraction": 0.02, "expand_joint": False},
+    {"persistence": 0.0, "expand_k": False, "expand_joint": False, "budget_scale": 0.9,
+     "exploration_fraction": 0.5},
+)
+
+
+def directional_inputs(c3):
+    """Masses and previous route of the directional fixtures (the tests rebuild
+    them the same way and check the digests)."""
+    heads = c3["heads"]
+    mass = torch.from_numpy(c3["mass_heads"])
+    prev = torch.from_numpy(np.unpackbits(c3["prev"], axis=-1, count=450).astype(bool))[heads]
+    quant = torch.round(mass * (450 * 64.0)) / (450 * 64.0)
+    return {"plain": mass, "quant": quant}, prev
+
+
+def directional():
+    c3 = np.load(HERE / "config3.npz")
+    masses, prev = directional_inputs(c3)
+    lay = ref_spatial.build_spatial_layout((16, 45, 80), block_size=128)
+    nb = lay.neighbors_cpu
+    backend = ref_flex.FlexReuseBackend(ref_flex.FlexReuseConfig(block_size=128))
+    arrays = {}
+    for mname, mass in masses.items():
+        arrays[f"{mname}_sha"] = sha256(mass)
+        for i, opts in enumerate(DIRECTIONAL_OPTIONS):
+            result = ref_routing.directional_budget_update(
+                mass, prev, nb, keep=0.625, previous_frontier=ref_routing.frontier_mask(prev, nb),
+                **opts)
+            for key, value in result.items():
+                arrays[f"{mname}{i}_{key}"] = packbits(value)
+            sunk = backend._add_first_frame_sink({"grid": (16, 45, 80), "layout": lay}, result)
+            arrays[f"{mname}{i}_sunk_route"] = packbits(sunk["route"])
+            arrays[f"{mname}{i}_sunk_frontier"] = packbits(sunk["frontier"])
+    arrays["options"] = np.array(json.dumps(DIRECTIONAL_OPTIONS))
+    np.savez_compressed(HERE / "directional.npz", **arrays)
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    for fn in (kat, layouts, config1, route_480p, blob_routes, config3):
+    only = set(sys.argv[1:])
+    for fn in (kat, layouts, config1, route_480p, blob_routes, config3, directional):
+        if only and fn.__name__ not in only:
+            continue
         t = time.time()
         fn()
         print(f"{fn.__name__}: {time.time() - t:.1f}s")

@@ -33,9 +33,22 @@ def test_config_validation_matches_reference(kwargs, message):
         FlexReuseBackend(FlexReuseConfig(**kwargs))
 
 
-def test_directional_update_is_not_built():
-    with pytest.raises(NotImplementedError):
-        FlexReuseBackend(FlexReuseConfig(directional_update=True, spatial_reorder=True))
+def test_directional_update_config_is_accepted():
+    backend = FlexReuseBackend(FlexReuseConfig(directional_update=True, spatial_reorder=True,
+                                               route_exploration_fraction=0.1))
+    assert backend.config.directional_update
+
+
+def test_directional_update_fails_loudly_on_cpu():
+    from dit_sparse_atten_b200 import routing
+
+    mass = torch.rand(1, 4, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        routing.directional_budget_update(mass, mass > 0.5, torch.full((4, 4), -1), keep=0.5)
+    with pytest.raises(ValueError, match="identical shapes"):
+        routing.directional_budget_update(mass, mass[0] > 0.5, torch.full((4, 4), -1), keep=0.5)
+    with pytest.raises(ValueError, match=r"neighbors must have shape \[blocks, 4\]"):
+        routing.directional_budget_update(mass, mass > 0.5, torch.full((3, 4), -1), keep=0.5)
 
 
 def test_first_frame_sink_is_added_to_every_query_row():
