@@ -99,6 +99,13 @@ def kept_flops(route, tokens, block, dim):
 # ----------------------------------------------------------------------------
 
 class ClockSampler:
+    """SM clocks and clock-event reasons of one GPU during the timed region.
+
+    Read-only NVML queries from a background thread every 20 ms, plus one
+    sample on entry and one on exit so that short regions are covered;
+    ``nvidia-smi -lms`` is the fallback when NVML is unavailable.
+    """
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -106,8 +113,46 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.samples = []            # (sm_mhz, max_mhz, set of reason names)
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except pynvml.NVMLError:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle,
+                                                                  pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def _sample(self):
+        n = self.nvml
+        sm = float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+        mask = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        self.samples.append((sm, self.max_mhz,
+                             {name for name, bit in self.bits.items() if mask & bit}))
+
+    def _loop(self):
+        while not self._stop.wait(0.02):
+            self._sample()
 
     def __enter__(self):
+        if self.nvml is not None:
+            import threading
+            self._sample()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -118,7 +163,11 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.nvml is not None:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -126,25 +175,24 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            for line in out.splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 7:
+                    continue
+                try:
+                    sm, mx = float(parts[0]), float(parts[1])
+                except ValueError:
+                    continue
+                self.samples.append((sm, mx, {name for name, val in zip(self.NAMES, parts[3:7])
+                                              if val.lower() == "active"}))
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in getattr(self, "lines", []):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        sm = [s[0] for s in self.samples]
+        reasons = set().union(*(s[2] for s in self.samples)) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": self.samples[-1][1] if self.samples else None,
+                "samples": len(sm), "reasons": sorted(reasons),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------
@@ -289,6 +337,23 @@ def main(argv=None):
 
     stream = torch.cuda.current_stream(device)
     attn_events = []
+    pipe = None
+    if P > 1 and len(branches) == 1:
+        # chunked exchange overlapped with the attention of earlier chunks
+        pipe = parallel.PipelinedHeadParallel(group, P, cfg.heads, t_local,
+                                              perm=layout.permutation_cpu,
+                                              inverse=layout.inverse_cpu)
+        hc = pipe.hc
+        chunk_csr = [(counts[:, c * hc:(c + 1) * hc].contiguous(),
+                      indices[:, c * hc:(c + 1) * hc].contiguous()) for c in range(pipe.chunks)]
+
+        def attend_chunk(qp, kp, vp, c):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out_p = kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block)
+            e1.record(stream)
+            attn_events.append((e0, e1))
+            return out_p
 
     def attend(qh, kh, vh):
         qp, kp, vp = layout.reorder_qkv(qh, kh, vh)
@@ -300,6 +365,8 @@ def main(argv=None):
         return layout.restore(out_p)
 
     def step():
+        if pipe is not None:
+            return pipe(q, k, v, attend_chunk)
         if P > 1:
             return parallel.head_parallel_attention(q, k, v, attend, group, P)
         return attend(q, k, v)
@@ -324,7 +391,7 @@ def main(argv=None):
         torch.cuda.synchronize()
     barrier()
     ms = start.elapsed_time(end) / args.steps
-    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_events)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_events) / args.steps
     _native.check_device_errors()
     rank_ms = None
     if world > 1:
@@ -389,11 +456,13 @@ def main(argv=None):
             * cfg.batch / (ms * 1e-3) / 1e12,
             "parallelism": ("single GPU" if world == 1 else
                             f"{plan.cfg_groups} CFG group(s) x {P}-way head parallel "
-                            "(Ulysses all-to-all, NCCL)"),
+                            "(Ulysses all-to-all, NCCL"
+                            + (f", {pipe.chunks} head chunks overlapped with attention)"
+                               if pipe is not None else ")")),
             "l2": "inputs (3 x 1.18 GB) exceed L2; no flush"},
         "stages": stages,
         "roofline": roofline,
-        "gpu_launches": 3 * args.steps * world,
+        "gpu_launches": 3 * args.steps * world * (pipe.chunks if pipe is not None else 1),
         **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),
     }

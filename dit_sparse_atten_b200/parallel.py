@@ -113,6 +113,107 @@ def head_parallel_attention(q, k, v, attend, group, group_size):
     return head_to_seq(out, group, group_size)
 
 
+def pipeline_chunks(heads_per_rank):
+    """Head chunks per rank for ``PipelinedHeadParallel``: 4, 2, 5 or 3 chunks
+    of at least 4 heads each (enough attention per chunk to hide the next
+    chunk's exchange), else 1."""
+    for c in (4, 2, 5, 3):
+        if heads_per_rank % c == 0 and heads_per_rank // c >= 4:
+            return c
+    return 1
+
+
+class PipelinedHeadParallel:
+    """Ulysses exchange in head chunks, overlapped with the attention.
+
+    For one CFG branch (batch 1) of sequence shards ``[1, T/P, H, D]``: this
+    rank's ``H/P`` heads are split into ``chunks`` groups.  The input
+    all-to-all of every chunk is issued up front on NCCL's stream; chunk c's
+    packed Q/K/V are gathered straight from its receive buffer (no
+    concatenation or transpose copies: the pack permutation is remapped onto
+    the receive layout ``[src rank, q|k|v, T/P, heads, D]``), ``attend`` runs
+    on them, the result is restored to token order - which is already the
+    send layout of the output all-to-all - and sent back while the next chunk
+    computes.  Only the first chunk's input exchange and the last chunk's
+    output exchange stay exposed.
+
+    ``attend(qp, kp, vp, chunk) -> out_p`` takes and returns ``[1, T, hc, D]``
+    tensors in pack order (for example the routed attention over the chunk's
+    heads' CSR).  ``gather(tensors, perm)`` is the row gather
+    (``kernels.reorder_rows`` on GPUs; CPU tests pass an ``index_select``).
+    """
+
+    def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
+                 chunks=None, gather=None):
+        if heads % group_size:
+            raise ValueError(f"{heads} heads do not split over {group_size} ranks")
+        self.group = group
+        self.P = group_size
+        self.hp = heads // group_size
+        self.chunks = chunks or pipeline_chunks(self.hp)
+        if self.hp % self.chunks:
+            raise ValueError(f"{self.hp} heads per rank do not split into {self.chunks} chunks")
+        self.hc = self.hp // self.chunks
+        self.tl = tokens_local
+        tokens = tokens_local * group_size
+        if (inverse is None) != (perm is None):
+            raise ValueError("give both perm and inverse, or neither")
+        perm = (torch.arange(tokens, dtype=torch.int64) if perm is None
+                else torch.as_tensor(perm).to("cpu", torch.int64))
+        if perm.numel() != tokens:
+            raise ValueError("perm must cover the whole sequence")
+        src, local = perm // tokens_local, perm % tokens_local
+        # row of token perm[i] of tensor 0 in the receive buffer viewed as
+        # [P * 3 * T/P] rows; tensor t starts t * T/P rows later
+        self._src_perm = (src * 3 * tokens_local + local).to(torch.int32)
+        self._inverse = None if inverse is None else torch.as_tensor(inverse).to(torch.int32)
+        self._dev = {}
+        if gather is None:
+            from . import kernels
+            gather = kernels.reorder_rows
+        self.gather = gather
+
+    def _device_tables(self, device):
+        if device not in self._dev:
+            self._dev[device] = (self._src_perm.to(device),
+                                 None if self._inverse is None else self._inverse.to(device))
+        return self._dev[device]
+
+    def __call__(self, q, k, v, attend):
+        b, tl, h, d = q.shape
+        if b != 1 or tl != self.tl or h != self.hp * self.P:
+            raise ValueError("PipelinedHeadParallel takes [1, T/P, H, D] shards of one branch")
+        P, hp, hc, C = self.P, self.hp, self.hc, self.chunks
+        src_perm, inverse = self._device_tables(q.device)
+        send = torch.empty((C, P, 3, tl, hc, d), dtype=q.dtype, device=q.device)
+        recv = torch.empty_like(send)
+        inputs = []
+        for c in range(C):
+            for t, x in enumerate((q, k, v)):
+                send[c, :, t].copy_(x[0].view(tl, P, hp, d)[:, :, c * hc:(c + 1) * hc]
+                                    .permute(1, 0, 2, 3))
+            inputs.append(dist.all_to_all_single(recv[c], send[c], group=self.group,
+                                                 async_op=True))
+        span = (3 * P - 2) * tl
+        outputs, sent = [], []
+        orecv = torch.empty((C, P, tl, hc, d), dtype=q.dtype, device=q.device)
+        for c in range(C):
+            inputs[c].wait()
+            flat = recv[c].view(1, P * 3 * tl, hc, d)
+            qp, kp, vp = self.gather([flat[:, t * tl:t * tl + span] for t in range(3)], src_perm)
+            out_p = attend(qp, kp, vp, c)
+            out_c = out_p if inverse is None else self.gather([out_p], inverse)[0]
+            sent.append(out_c)
+            outputs.append(dist.all_to_all_single(orecv[c], out_c.view(P, tl, hc, d),
+                                                  group=self.group, async_op=True))
+        out = torch.empty_like(q)
+        for c in range(C):
+            outputs[c].wait()
+            out[0].view(tl, P, hp, d)[:, :, c * hc:(c + 1) * hc].copy_(
+                orecv[c].permute(1, 0, 2, 3))
+        return out
+
+
 def all_reduce_count(count, group=None):
     """Sum an integer count over the group (the dense-dispatch keep numerator)."""
     t = count.clone() if torch.is_tensor(count) else torch.tensor([int(count)])

@@ -102,8 +102,8 @@ def test_empty_rows_are_zero_and_lse():
 
 
 def test_many_items_per_cta_with_empty_rows():
-    """More (b, h, qb) work items than query tiles in flight on the GPU (each
-    persistent CTA walks several), empty routes among them, a partial tail."""
+    """More (b, h, qb) work items than CTAs resident on the GPU at once (later
+    CTAs start as earlier ones retire), empty routes among them, a partial tail."""
     g = torch.Generator().manual_seed(9)
     B, H, T = 2, 4, 128 * 100 - 5
     blocks = math.ceil(T / 128)

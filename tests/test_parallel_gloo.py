@@ -77,6 +77,51 @@ def _attention(rank, world):
     return True
 
 
+def _cpu_gather(tensors, perm):
+    return tuple(t.index_select(1, perm.long()) for t in tensors)
+
+
+def _pipelined(rank, world):
+    q, k, v = full_inputs()
+    t = q.shape[1] // world
+    sl = slice(rank * t, (rank + 1) * t)
+    perm = torch.randperm(q.shape[1], generator=torch.Generator().manual_seed(3))
+    inverse = torch.empty_like(perm)
+    inverse[perm] = torch.arange(perm.numel())
+    seen = []
+
+    def sdpa(qh, kh, vh):
+        return torch.nn.functional.scaled_dot_product_attention(
+            qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2)).transpose(1, 2)
+
+    def attend(qp, kp, vp, chunk):
+        seen.append(chunk)
+        return sdpa(qp, kp, vp)         # permutation-equivariant: output stays in pack order
+
+    ref = sdpa(q, k, v)[:, sl]
+    for kw in ({"perm": perm, "inverse": inverse, "chunks": 2}, {"chunks": 1}, {"chunks": 2}):
+        seen.clear()
+        pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, q.shape[2], t,
+                                              gather=_cpu_gather, **kw)
+        out = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), attend)
+        torch.testing.assert_close(out, ref)
+        assert seen == list(range(kw["chunks"]))
+    # the packed inputs of a chunk are exactly this rank's heads in pack order
+    got = {}
+
+    def capture(qp, kp, vp, chunk):
+        got[chunk] = qp.clone()
+        return qp
+    pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, q.shape[2], t, perm=perm,
+                                          inverse=inverse, chunks=2, gather=_cpu_gather)
+    pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), capture)
+    hp = q.shape[2] // world
+    for c in range(2):
+        head = rank * hp + c
+        assert torch.equal(got[c][0, :, 0], q[0, perm, head])
+    return True
+
+
 def _keep(rank, world):
     from dit_sparse_atten_b200.flex import FlexReuseBackend
     backend = FlexReuseBackend(process_group=dist.group.WORLD)
@@ -90,6 +135,18 @@ def test_seq_head_exchange_round_trip():
 
 def test_head_parallel_attention_equals_full():
     assert all(run_ranks(_attention).values())
+
+
+def test_pipelined_exchange_equals_full_attention():
+    assert all(run_ranks(_pipelined).values())
+
+
+def test_pipeline_chunk_rule():
+    assert [parallel.pipeline_chunks(h) for h in (40, 20, 10, 5, 8, 12)] == [4, 4, 2, 1, 2, 2]
+    with pytest.raises(ValueError):
+        parallel.PipelinedHeadParallel(None, 2, 40, 16, chunks=3)
+    with pytest.raises(ValueError):
+        parallel.PipelinedHeadParallel(None, 2, 40, 16, perm=torch.arange(32))
 
 
 def test_keep_fraction_is_global():
