@@ -436,6 +436,7 @@ def main(argv=None):
         if not args.no_route_stage:
             stages.update(route_stage(cfg, qp, kp, local_route, kernels, device, stream,
                                       layout.neighbors(device)))
+            stages.update(bootstrap_stage(cfg, qp, kp, vp, kernels, stream))
 
     peaks, peak_src = load_peaks()
     local_flops = kept_flops(local_route, cfg.tokens, cfg.block, cfg.head_dim)
@@ -514,6 +515,8 @@ def route_stage(cfg, qp, kp, route, kernels, device, stream, neighbors):
     dev[1].record(stream)
     torch.cuda.synchronize()
     directional_ms = dev[0].elapsed_time(dev[1])
+    from dit_sparse_atten_b200 import _native
+    _native.check_device_errors()   # a timed-out wait must not pass as a timing
     B, H, Qb = mass.shape[0], mass.shape[1], mass.shape[2]
     # mass 4 + previous 1 + frontier 1 + candidates 3 (clear, scatter, final)
     # + route/frontier/exploration/dropped/added 5 + CSR ids 4 bytes per cell
@@ -526,6 +529,30 @@ def route_stage(cfg, qp, kp, route, kernels, device, stream, neighbors):
             "directional_update_ms": directional_ms,
             "directional_update_hbm_gbs": directional_bytes / directional_ms / 1e6,
             "route_mass_hbm_gbs": (sampled + B * H * Qb * Qb * 4) / mass_ms / 1e6}
+
+
+def bootstrap_stage(cfg, qp, kp, vp, kernels, stream):
+    """Exact bootstrap of this layer (flex.py:254-272): dense attention over all
+    blocks with its LSE, then the exact block mass from that LSE."""
+    from dit_sparse_atten_b200 import _native
+    from dit_sparse_atten_b200.flex import _dense_with_lse
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for i in range(2):
+        if i == 1:
+            ev[0].record(stream)
+        _, lse = _dense_with_lse(qp, kp, vp, cfg.block)
+        if i == 1:
+            ev[1].record(stream)
+        kernels.exact_block_mass(qp, kp, cfg.block, lse=lse)
+    ev[2].record(stream)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    dense_ms, mass_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    B, T, H, D = qp.shape
+    exps = B * H * T * T
+    return {"bootstrap_dense_ms": dense_ms, "bootstrap_exact_mass_ms": mass_ms,
+            "bootstrap_dense_tflops": 4.0 * B * H * T * T * D / dense_ms / 1e9,
+            "bootstrap_exact_mass_gexp_per_s": exps / mass_ms / 1e6}
 
 
 def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total_flops):

@@ -400,8 +400,8 @@ int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_
 }
 
 int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t tokens,
-                         int64_t heads, int32_t head_dim, int32_t block, float scale, float* mass,
-                         int32_t* err_word, void* stream) {
+                         int64_t heads, int32_t head_dim, int32_t block, float scale,
+                         const float* lse, float* mass, int32_t* err_word, void* stream) {
   if (q == nullptr || k == nullptr || mass == nullptr || err_word == nullptr)
     return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
@@ -430,6 +430,7 @@ int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t to
   a.round_bf16 = 0;
   a.block_bias = nullptr;
   a.mass_scale = 1.0f;
+  a.lse = lse;
   a.mass = mass;
   a.err_word = err_word;
   cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, static_cast<cudaStream_t>(stream));

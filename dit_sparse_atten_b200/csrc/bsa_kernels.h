@@ -76,6 +76,7 @@ struct MassArgs {
   int32_t round_bf16;
   const float* block_bias;        // [Qb] additive key weight per key block, or null (0)
   float mass_scale;               // multiplies each block sum (1/S: mean over query samples)
+  const float* lse;               // [B, H, n_rows] natural-log LSE per query row, or null
   float* mass;                    // [B, H, Qb, Qb]
   int* err_word;
 };

@@ -1,26 +1,28 @@
-// (b) Sampled block mass on tcgen05.
+// (b) Block mass on tcgen05: the sampled mass of the route update and the
+// exact mass of the dense bootstrap.
 //
-// Reference semantics: attention_backends/flex.py:205-251.  For every head,
-// the sampled queries ([Qb*S, D], S evenly spaced tokens per block) attend to
-// all sampled keys ([Qb*S, D]) with an additive per-key weight
-// log(block_size / S); the softmax row is then summed over the S key samples of
-// each key block and averaged over the S query samples of each query block:
+// Sampled (attention_backends/flex.py:205-251): for every head, the sampled
+// queries ([Qb*S, D], S evenly spaced tokens per block) attend to all sampled
+// keys ([Qb*S, D]) with an additive per-key weight log(block_size / S); the
+// softmax row is then summed over the S key samples of each key block and
+// averaged over the S query samples of each query block:
 //   mass[h, qb, kb] = (1/S) * sum_{r in qb} sum_{k in kb} softmax_r(k).
 // With round_bf16 set, scores are rounded like the reference's bf16 matmul
 // output and bf16 `* score_scale` (flex.py:245) before the fp32 softmax.
 //
-// One CTA per (128 sampled query rows, head, batch).  The 128-key tiles of the
-// sampled keys stream twice through a TMA ring: pass 1 computes every row's
-// log-sum-exp, pass 2 the normalised per-block sums (S consecutive rows of a
-// query block are S consecutive lanes, reduced with shuffles).
-//   warp 4 TMA producer, warp 5 TMEM allocator + tcgen05.mma issuer,
-//   warps 0-3 softmax / reduction (thread i owns sampled row i).
+// Exact (flex.py:97-108,167-202): the same with S = block over all tokens,
+// no weights, no rounding and no mean: the probability summed over each
+// block x block tile.  Given the per-query log-sum-exp of the dense pass
+// (MassArgs::lse) only the second pass runs, as in the reference.
+//
+// One CTA per (128 query rows, head, batch).  The 128-key tiles stream through
+// a TMA ring: pass 1 computes every row's log-sum-exp, pass 2 the normalised
+// per-block sums.
 #include "bsa_kernels.h"
 
 namespace bsa {
 namespace {
 
-constexpr int kMassThreads = 192;
 constexpr int kSlots = 5;
 constexpr int kTile = 128;
 constexpr float kLog2eM = 1.4426950408889634f;
@@ -30,8 +32,6 @@ constexpr int kPanel = kTile * 128;
 constexpr int kRingOff = kQBytes;
 constexpr int kBiasOff = kRingOff + kSlots * kSlotBytes;
 constexpr int kMaxBlocks = 4096;
-constexpr int kBarOff = kBiasOff + kMaxBlocks * 4;
-constexpr int kMassSmem = kBarOff + 256 + 1024;
 
 struct MassBarriers {
   uint64_t q_full;
@@ -40,214 +40,14 @@ struct MassBarriers {
   uint64_t drain;
   uint64_t slot_full[kSlots];
   uint64_t slot_empty[kSlots];
+  uint64_t red_full[2];   // S > 32: eight warps' partials of a group of tiles written
+  uint64_t red_free[2];   // S > 32: the group's slots summed and free again
   uint32_t tmem_base;
   int abort;
 };
 
-template <int LOG2S>
-__global__ void __launch_bounds__(kMassThreads, 1)
-    sampled_mass_kernel(const __grid_constant__ CUtensorMap tm_q,
-                        const __grid_constant__ CUtensorMap tm_k, const MassArgs a) {
-  constexpr int S = 1 << LOG2S;
-  constexpr int kGroups = kTile / S;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sRing = smem + kRingOff;
-  float* sBias = reinterpret_cast<float*>(smem + kBiasOff);
-  __shared__ float sRed[8];
-  MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + kBarOff);
-  volatile int* abort_flag = &bar->abort;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int qt = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int n_tiles = static_cast<int>((a.n_rows + kTile - 1) / kTile);
-  const int steps = 2 * n_tiles;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->s_free[i], 128);
-    }
-    mbar_init(&bar->drain, 1);
-    for (int s = 0; s < kSlots; ++s) {
-      mbar_init(&bar->slot_full[s], 1);
-      mbar_init(&bar->slot_empty[s], 1);
-    }
-    bar->abort = prior_timeout(a.err_word) ? 1 : 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (bar->abort) return;  // uniform: set before the barrier, read after it
-  for (int i = threadIdx.x; i < a.q_blocks; i += kMassThreads)
-    sBias[i] = a.block_bias != nullptr ? a.block_bias[i] : 0.f;
-  if (warp == 5) tmem_alloc(&bar->tmem_base, 256);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = bar->tmem_base;
-
-  if (warp == 4) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      mbar_arrive_expect_tx(&bar->q_full, kQBytes);
-      tma_load_4d(sQ, &tm_q, &bar->q_full, 0, h, qt * kTile, b);
-      tma_load_4d(sQ + kPanel, &tm_q, &bar->q_full, 64, h, qt * kTile, b);
-      uint32_t armed = 0, armed_phase = 0;  // per slot: a load was issued / its parity
-      for (int i = 0; i < steps; ++i) {
-        const int s = i % kSlots;
-        const uint32_t ph = (i / kSlots) & 1;
-        if (!mbar_wait(&bar->slot_empty[s], ph ^ 1, abort_flag, a.err_word)) break;
-        const int kt = i % n_tiles;
-        uint8_t* dst = sRing + s * kSlotBytes;
-        mbar_arrive_expect_tx(&bar->slot_full[s], kSlotBytes);
-        tma_load_4d(dst, &tm_k, &bar->slot_full[s], 0, h, kt * kTile, b);
-        tma_load_4d(dst + kPanel, &tm_k, &bar->slot_full[s], 64, h, kt * kTile, b);
-        armed |= 1u << s;
-        armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
-      }
-      int never = 0;
-      mbar_wait(&bar->q_full, 0, &never, a.err_word);
-#pragma unroll
-      for (int s = 0; s < kSlots; ++s)
-        if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
-    }
-  } else if (warp == 5) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(128, kTile, false);
-      const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t ring_addr = smem_u32(sRing);
-      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
-      for (int i = 0; ok && i < steps; ++i) {
-        const int s = i % kSlots;
-        ok = mbar_wait(&bar->slot_full[s], (i / kSlots) & 1, abort_flag, a.err_word);
-        if (ok && i >= 2) ok = mbar_wait(&bar->s_free[i & 1], ((i >> 1) - 1) & 1, abort_flag, a.err_word);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t k_addr = ring_addr + s * kSlotBytes;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          const uint64_t da = sdesc_sw128(q_addr + (kk >> 2) * kPanel + off, 16, 1024);
-          const uint64_t db = sdesc_sw128(k_addr + (kk >> 2) * kPanel + off, 16, 1024);
-          umma_bf16_ss(tmem + (i & 1) * 128, da, db, idesc, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&bar->s_full[i & 1]);
-        umma_commit(&bar->slot_empty[s]);
-      }
-      int never = 0;
-      umma_commit(&bar->drain);
-      mbar_wait(&bar->drain, 0, &never, a.err_word);
-    }
-  } else {
-    const int row = threadIdx.x;
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    const int64_t qrow = static_cast<int64_t>(qt) * kTile + row;
-    float m2 = -INFINITY, l = 0.f, inv_l = 0.f;
-    bool ok = true;
-    for (int i = 0; i < steps; ++i) {
-      ok = mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.err_word);
-      if (!ok) break;
-      tc_fence_after();
-      float y[kTile];
-      uint32_t r[kTile];
-#pragma unroll
-      for (int cc = 0; cc < kTile / 32; ++cc)
-        tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + cc * 32, r + cc * 32);
-      tmem_wait_ld();
-      reg_fence<kTile>(r);
-#pragma unroll
-      for (int x = 0; x < kTile; ++x) y[x] = __uint_as_float(r[x]);
-      tc_fence_before();
-      mbar_arrive(&bar->s_free[i & 1]);
-      const int kt = i % n_tiles;
-      const int64_t key0 = static_cast<int64_t>(kt) * kTile;
-#pragma unroll
-      for (int x = 0; x < kTile; ++x) {
-        float sc = y[x];
-        if (a.round_bf16) sc = round_to_bf16(round_to_bf16(sc) * a.scale);
-        else sc = sc * a.scale;
-        const int64_t key = key0 + x;
-        y[x] = key < a.n_rows ? (sc + sBias[key >> LOG2S]) * kLog2eM : -INFINITY;
-      }
-      if (i < n_tiles) {
-        float mx = y[0];
-#pragma unroll
-        for (int x = 1; x < kTile; ++x) mx = fmaxf(mx, y[x]);
-        const float m_new = fmaxf(m2, mx);
-        float rs = 0.f;
-#pragma unroll
-        for (int x = 0; x < kTile; ++x) rs += ex2_approx(y[x] - m_new);
-        l = l * ex2_approx(m2 - m_new) + rs;
-        m2 = m_new;
-        if (i == n_tiles - 1) inv_l = 1.f / l;
-      } else {
-        float g[kGroups];
-#pragma unroll
-        for (int gi = 0; gi < kGroups; ++gi) {
-          float acc = 0.f;
-#pragma unroll
-          for (int x = 0; x < S; ++x) acc += ex2_approx(y[gi * S + x] - m2);
-          g[gi] = qrow < a.n_rows ? acc * inv_l : 0.f;
-        }
-        if constexpr (S > 1) {
-#pragma unroll
-          for (int gi = 0; gi < kGroups; ++gi) {
-#pragma unroll
-            for (int off = 1; off < (S < 32 ? S : 32); off <<= 1)
-              g[gi] += __shfl_xor_sync(0xffffffffu, g[gi], off);
-          }
-        }
-        const int64_t kb0 = key0 >> LOG2S;
-        const int64_t out_rows = (static_cast<int64_t>(b) * a.heads + h) * a.q_blocks;
-        if constexpr (S <= 32) {
-          const int64_t qblock = qrow >> LOG2S;
-          if ((row & (S - 1)) == 0 && qblock < a.q_blocks) {
-            float* dst = a.mass + (out_rows + qblock) * a.q_blocks;
-#pragma unroll
-            for (int gi = 0; gi < kGroups; ++gi)
-              if (kb0 + gi < a.q_blocks) dst[kb0 + gi] = g[gi] * a.mass_scale;
-          }
-        } else {
-          // A query block spans S/32 warps: combine the warp sums in shared
-          // memory (softmax warps only, named barrier 1).
-          if (lane == 0)
-#pragma unroll
-            for (int gi = 0; gi < kGroups; ++gi) sRed[warp * kGroups + gi] = g[gi];
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          constexpr int kWarpsPerBlock = S / 32;
-          if (row < (4 / kWarpsPerBlock) * kGroups) {
-            const int qsub = row / kGroups;
-            const int gi = row % kGroups;
-            float acc = 0.f;
-            for (int w = 0; w < kWarpsPerBlock; ++w) acc += sRed[(qsub * kWarpsPerBlock + w) * kGroups + gi];
-            const int64_t qblock = (static_cast<int64_t>(qt) * kTile >> LOG2S) + qsub;
-            if (qblock < a.q_blocks && kb0 + gi < a.q_blocks)
-              a.mass[(out_rows + qblock) * a.q_blocks + kb0 + gi] = acc * a.mass_scale;
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
-      }
-    }
-    (void)ok;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 256);
-  }
-}
-
 // ---------------------------------------------------------------------------
-// S <= 32 (the sampled route, and the exact mass at 32-token blocks).  Eight
-// softmax warps, two per SM sub-partition: warp w owns rows 32*(w%4).. and
+// Eight softmax warps, two per SM sub-partition: warp w owns rows 32*(w%4).. and
 // column half w/4 of every S tile, keeps its own running (max, sum) over its
 // half-rows in pass 1 and combines it with the other half once, through
 // shared memory, before pass 2.  All score arithmetic is packed (f32x2); the
@@ -255,12 +55,19 @@ __global__ void __launch_bounds__(kMassThreads, 1)
 // split between the conversion unit (the first) and the FMA pipe (the second,
 // by Veltkamp splitting), so that neither pipe carries both next to the
 // exponentials; a share of the exponentials runs on the FMA pipe too
-// (exp2_poly2).  A query block's S sampled rows are S consecutive lanes,
-// reduced with shuffles.
+// (exp2_poly2).  For S <= 32 a query block's S rows are S consecutive lanes,
+// reduced with shuffles.  For S = 64, 128 (exact mass) a query block spans
+// several warps: each warp sums its 32 rows with shuffles and writes one
+// partial per key tile into shared memory; every kRedTiles tiles warp 0 adds
+// the eight partials in a fixed order (deterministic) and writes the mass.
+// The hand-over uses mbarriers with bounded waits (red_full / red_free,
+// double-buffered).
 //   warp 8 TMA producer, warp 9 TMEM allocator + tcgen05.mma issuer.
 constexpr int kMass2Threads = 320;
+constexpr int kRedTiles = 16;
 constexpr int kXchgOff = kBiasOff + kMaxBlocks * 4;
-constexpr int kBar2Off = kXchgOff + 2 * 128 * 2 * 4;
+constexpr int kRedOff = kXchgOff + 2 * 128 * 2 * 4;           // [2][kRedTiles][8] floats
+constexpr int kBar2Off = kRedOff + 2 * kRedTiles * 8 * 4;
 constexpr int kMass2Smem = kBar2Off + 256 + 1024;
 constexpr int kMassEmulated = 2;  // of every 8 column pairs, exponentials on the FMA pipe
 
@@ -331,8 +138,9 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
     sampled_mass_kernel2(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k, const MassArgs a) {
   constexpr int S = 1 << LOG2S;
-  constexpr int kHalfBlocks = 64 / S;  // key blocks in a 64-column half tile
-  static_assert(S <= 32, "a query block's rows must fit in one warp");
+  constexpr bool kWide = S > 32;              // a query block spans several warps
+  constexpr int kHalfBlocks = kWide ? 1 : 64 / S;  // key blocks in a 64-column half tile
+  static_assert(S <= 128, "at most 128 rows per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -340,6 +148,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   uint8_t* sRing = smem + kRingOff;
   float* sBiasL = reinterpret_cast<float*>(smem + kBiasOff);
   float2* sX = reinterpret_cast<float2*>(smem + kXchgOff);  // [half][row] (max, sum)
+  float* sRed = reinterpret_cast<float*>(smem + kRedOff);    // [buf][tile][warp] (S > 32)
   MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + kBar2Off);
   volatile int* abort_flag = &bar->abort;
 
@@ -349,13 +158,17 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int n_tiles = static_cast<int>((a.n_rows + kTile - 1) / kTile);
-  const int steps = 2 * n_tiles;
+  // With the log-sum-exp given, pass 1 is skipped.
+  const int pass1 = a.lse != nullptr ? 0 : n_tiles;
+  const int steps = pass1 + n_tiles;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
       mbar_init(&bar->s_free[i], 256);
+      mbar_init(&bar->red_full[i], 8);
+      mbar_init(&bar->red_free[i], 1);
     }
     mbar_init(&bar->drain, 1);
     for (int s = 0; s < kSlots; ++s) {
@@ -434,8 +247,15 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
     const int64_t qrow = static_cast<int64_t>(qt) * kTile + row;
     const int64_t out_rows = (static_cast<int64_t>(b) * a.heads + h) * a.q_blocks;
     float m2 = -INFINITY, l = 0.f, m_fold = 0.f;
+    if (a.lse != nullptr && qrow < a.n_rows)
+      m_fold = a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.n_rows + qrow] * kLog2eM;
+    bool combined = pass1 == 0;   // pass 1's two half-rows met (named barrier 1 + wq)
+    bool ok = true;
     for (int i = 0; i < steps; ++i) {
-      if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.err_word)) break;
+      if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.err_word)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t r[64];
       tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + half * 64, r);
@@ -447,7 +267,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
       const int64_t key0 = static_cast<int64_t>(i % n_tiles) * kTile + half * 64;
       float2 y[32];
       mass_scores<LOG2S, kRound>(r, y, key0, a.n_rows, sBiasL, a.scale);
-      if (i < n_tiles) {
+      if (i < pass1) {
         // Pass 1: running max and sum of this half-row.
         float m8[8];
 #pragma unroll
@@ -481,6 +301,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
           // named barrier 1 + wq.
           sX[half * 128 + row] = make_float2(m2, l);
           asm volatile("bar.sync %0, 64;" ::"r"(1 + wq) : "memory");
+          combined = true;
           const float2 o = sX[(half ^ 1) * 128 + row];
           const float m_all = fmaxf(m2, o.x);
           const float l_all = l * ex2_approx(m2 - m_all) + o.y * ex2_approx(o.x - m_all);
@@ -509,23 +330,77 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
 #pragma unroll
           for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
         }
-        if constexpr (S > 1) {
+        if constexpr (!kWide) {
+          if constexpr (S > 1) {
 #pragma unroll
-          for (int gi = 0; gi < kHalfBlocks; ++gi) {
+            for (int gi = 0; gi < kHalfBlocks; ++gi) {
 #pragma unroll
-            for (int off = 1; off < S; off <<= 1) g[gi] += __shfl_xor_sync(0xffffffffu, g[gi], off);
+              for (int off = 1; off < S; off <<= 1)
+                g[gi] += __shfl_xor_sync(0xffffffffu, g[gi], off);
+            }
           }
-        }
-        const int64_t qblock = qrow >> LOG2S;
-        const int64_t kb0 = key0 >> LOG2S;
-        if ((lane & (S - 1)) == 0 && qblock < a.q_blocks) {
-          float* dst = a.mass + (out_rows + qblock) * a.q_blocks;
+          const int64_t qblock = qrow >> LOG2S;
+          const int64_t kb0 = key0 >> LOG2S;
+          if ((lane & (S - 1)) == 0 && qblock < a.q_blocks) {
+            float* dst = a.mass + (out_rows + qblock) * a.q_blocks;
 #pragma unroll
-          for (int gi = 0; gi < kHalfBlocks; ++gi)
-            if (kb0 + gi < a.q_blocks) dst[kb0 + gi] = g[gi] * a.mass_scale;
+            for (int gi = 0; gi < kHalfBlocks; ++gi)
+              if (kb0 + gi < a.q_blocks) dst[kb0 + gi] = g[gi] * a.mass_scale;
+          }
+        } else {
+          // This warp's 32 rows, then the eight warps' partials of the tile.
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) g[0] += __shfl_xor_sync(0xffffffffu, g[0], off);
+          const int t2 = i - pass1;                    // key tile of pass 2
+          const int grp_i = t2 / kRedTiles, slot = t2 % kRedTiles, buf = grp_i & 1;
+          if (slot == 0 && grp_i >= 2 &&
+              !mbar_wait(&bar->red_free[buf], ((grp_i >> 1) - 1) & 1, abort_flag, a.err_word)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) sRed[(buf * kRedTiles + slot) * 8 + warp] = g[0];
+          const bool last = slot == kRedTiles - 1 || t2 == n_tiles - 1;
+          if (last) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->red_full[buf]);
+          }
+          if (last && warp == 0) {
+            if (!mbar_wait(&bar->red_full[buf], (grp_i >> 1) & 1, abort_flag, a.err_word)) {
+              ok = false;
+              break;
+            }
+            if (lane <= slot) {
+              const float* pr = sRed + (buf * kRedTiles + lane) * 8;
+              const int64_t kt = static_cast<int64_t>(grp_i) * kRedTiles + lane;
+              if constexpr (S == 128) {
+                // warps: half * 4 + row quarter; one query and one key block
+                float v = pr[0];
+#pragma unroll
+                for (int w = 1; w < 8; ++w) v += pr[w];
+                if (qt < a.q_blocks && kt < a.q_blocks)
+                  a.mass[(out_rows + qt) * a.q_blocks + kt] = v * a.mass_scale;
+              } else {
+                // S = 64: query block 2 qt + (quarter >> 1), key block 2 kt + half
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  const int qbl = c >> 1, kbl = c & 1;
+                  const float v = pr[kbl * 4 + 2 * qbl] + pr[kbl * 4 + 2 * qbl + 1];
+                  const int64_t qb = 2 * static_cast<int64_t>(qt) + qbl, kb = 2 * kt + kbl;
+                  if (qb < a.q_blocks && kb < a.q_blocks)
+                    a.mass[(out_rows + qb) * a.q_blocks + kb] = v * a.mass_scale;
+                }
+              }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->red_free[buf]);
+          }
         }
       }
     }
+    // A warp that left pass 1 early (a timed-out wait) still arrives at the
+    // half-row barrier, so that the other warp of these rows is not held there.
+    if (!combined) asm volatile("bar.arrive %0, 64;" ::"r"(1 + wq) : "memory");
+    (void)ok;
   }
   tc_fence_before();
   __syncthreads();
@@ -533,25 +408,6 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
-}
-
-template <int LOG2S>
-cudaError_t launch_log2s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
-                         cudaStream_t stream) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    e = cudaFuncSetAttribute(sampled_mass_kernel<LOG2S>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMassSmem);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
-  const dim3 grid(static_cast<unsigned>((a.n_rows + kTile - 1) / kTile),
-                  static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  sampled_mass_kernel<LOG2S><<<grid, kMassThreads, kMassSmem, stream>>>(tq, tk, a);
-  return cudaGetLastError();
 }
 
 template <int LOG2S, bool kRound>
@@ -574,7 +430,7 @@ cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const 
 }
 
 template <int LOG2S>
-cudaError_t launch_small_s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
+cudaError_t launch_s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                            cudaStream_t stream) {
   return a.round_bf16 ? launch_log2s_v2<LOG2S, true>(tq, tk, a, stream)
                       : launch_log2s_v2<LOG2S, false>(tq, tk, a, stream);
@@ -587,14 +443,14 @@ cudaError_t launch_sampled_mass(const CUtensorMap& tq, const CUtensorMap& tk, co
   if (a.batch == 0 || a.heads == 0 || a.n_rows == 0) return cudaSuccess;
   if (a.q_blocks > kMaxBlocks) return cudaErrorInvalidValue;
   switch (a.samples) {
-    case 1: return launch_small_s<0>(tq, tk, a, stream);
-    case 2: return launch_small_s<1>(tq, tk, a, stream);
-    case 4: return launch_small_s<2>(tq, tk, a, stream);
-    case 8: return launch_small_s<3>(tq, tk, a, stream);
-    case 16: return launch_small_s<4>(tq, tk, a, stream);
-    case 32: return launch_small_s<5>(tq, tk, a, stream);
-    case 64: return launch_log2s<6>(tq, tk, a, stream);
-    case 128: return launch_log2s<7>(tq, tk, a, stream);
+    case 1: return launch_s<0>(tq, tk, a, stream);
+    case 2: return launch_s<1>(tq, tk, a, stream);
+    case 4: return launch_s<2>(tq, tk, a, stream);
+    case 8: return launch_s<3>(tq, tk, a, stream);
+    case 16: return launch_s<4>(tq, tk, a, stream);
+    case 32: return launch_s<5>(tq, tk, a, stream);
+    case 64: return launch_s<6>(tq, tk, a, stream);
+    case 128: return launch_s<7>(tq, tk, a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

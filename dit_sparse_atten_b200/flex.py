@@ -87,12 +87,15 @@ def _sampled_block_mass(q, k, block_size, samples=2, scale=None, query_block_chu
 def _block_attention_mass(q, k, lse=None, block_size=128, scale=None):
     """Exact dense block mass ``[H, Qb, Kb]`` (``flex.py:167-202``).
 
-    The kernel recomputes the per-row log-sum-exp itself, so ``lse`` is only
-    accepted for signature compatibility.
+    ``lse`` ``[1, H, T]`` (or ``[H, T]``) is the dense pass's per-query
+    log-sum-exp, as in the reference; without it the kernel computes it in a
+    first pass over the keys.
     """
     if q.shape[0] != 1 or q.shape[1] != k.shape[1]:
         raise ValueError("Flex bootstrap supports batch-1 self-attention")
-    return kernels.exact_block_mass(q, k, block_size, scale)[0]
+    if lse is not None and lse.dim() == 2:
+        lse = lse.unsqueeze(0)
+    return kernels.exact_block_mass(q, k, block_size, scale, lse=lse)[0]
 
 
 def _pack_route(route):
@@ -132,13 +135,42 @@ def _flex_output(q, k, v, block_mask, block_size, compile_kernel=True, scale=Non
     return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size, scale=scale)
 
 
+_FULL_ROUTES = {}
+
+
+def _full_route(heads, blocks, device):
+    """CSR of the all-blocks route ``[H, Qb]`` / ``[H, Qb, Qb]`` (cached)."""
+    key = (heads, blocks, torch.device(device))
+    if key not in _FULL_ROUTES:
+        if len(_FULL_ROUTES) > 8:
+            _FULL_ROUTES.clear()
+        _FULL_ROUTES[key] = kernels.pack_boolean_rows(
+            torch.ones((heads, blocks, blocks), dtype=torch.bool, device=device))
+    return _FULL_ROUTES[key]
+
+
+def _dense_with_lse(q, k, v, block_size, scale=None):
+    """Dense attention and its per-query log-sum-exp ``[1, H, T]`` in one kernel:
+    the routed attention over the all-blocks route (the reference's dense
+    FlexAttention call with ``return_lse=True``, ``flex.py:260-265``).  Returns
+    ``(None, None)`` for inputs the kernel does not take (not bf16 / D != 128)."""
+    if q.dtype != torch.bfloat16 or q.shape[-1] != kernels.HEAD_DIM or not q.is_cuda:
+        return None, None
+    counts, indices = _full_route(q.shape[2], math.ceil(q.shape[1] / block_size), q.device)
+    return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size,
+                                          scale=scale, return_lse=True)
+
+
 def _dense_bootstrap(q, k, v, block_size, mass_target, keep, compile_kernel, scale=None):
-    """Dense output and its exact block top-mass route (``flex.py:254-272``)."""
+    """Dense output and its exact block top-mass route (``flex.py:254-272``):
+    one attention pass that also returns the LSE, then one mass pass."""
     if q.shape[0] != 1 or q.shape[1] != k.shape[1]:
         raise ValueError("Flex bootstrap supports batch-1 self-attention")
     del compile_kernel
-    output = DenseBackend()(q, k, v, softmax_scale=scale, dtype=q.dtype)
-    mass = _block_attention_mass(q, k, None, block_size, scale=scale)
+    output, lse = _dense_with_lse(q, k, v, block_size, scale)
+    if output is None:
+        output = DenseBackend()(q, k, v, softmax_scale=scale, dtype=q.dtype)
+    mass = _block_attention_mass(q, k, lse, block_size, scale=scale)
     return output, _top_mass_route(mass, mass_target, keep)
 
 
@@ -335,9 +367,18 @@ class FlexReuseBackend:
             result["frontier"] = frontier_mask(route, layout.neighbors(route.device))
         return result
 
-    def _exact_route(self, state, q, k, softmax_scale):
+    def _dense_for_exact_route(self, q, k, v, softmax_scale, dense_only):
+        """Dense output plus the LSE the exact mass pass reuses (one attention
+        kernel over the all-blocks route), or SDPA and no LSE for inputs that
+        kernel does not take."""
+        output, lse = _dense_with_lse(q, k, v, self.config.block_size, softmax_scale)
+        if output is None:
+            return self.dense(q, k, v, **dense_only), None
+        return output, lse
+
+    def _exact_route(self, state, q, k, softmax_scale, lse=None):
         c = self.config
-        mass = _block_attention_mass(q, k, None, c.block_size, scale=softmax_scale)
+        mass = _block_attention_mass(q, k, lse, c.block_size, scale=softmax_scale)
         result = kernels.route_select(mass, target=c.mass_target, keep=c.keep,
                                       sink_blocks=self._sink_blocks(state))
         return self._result_from_csr(state, result, q.shape[1])
@@ -472,9 +513,9 @@ class FlexReuseBackend:
             state = {"route": None, "frontier": None, "block_mask": None, "step": step,
                      "layout": layout, "grid": grid}
             if self.config.bootstrap_mode == "exact":
-                output = self.dense(q, k, v, **dense_only)
+                output, lse = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
                 self.state[key] = state
-                self._install_route(state, self._exact_route(state, q, k, softmax_scale),
+                self._install_route(state, self._exact_route(state, q, k, softmax_scale, lse),
                                     q.shape[1])
                 self._update_dispatch(state)
                 self.phase_counts["dense_bootstrap"] += 1
@@ -506,8 +547,9 @@ class FlexReuseBackend:
         if (self.config.update_interval > 0
                 and (step - state["step"]) >= self.config.update_interval
                 and not self._is_final_step(step)):
-            output = self.dense(q, k, v, **dense_only)
-            self._install_route(state, self._exact_route(state, q, k, softmax_scale), q.shape[1])
+            output, lse = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
+            self._install_route(state, self._exact_route(state, q, k, softmax_scale, lse),
+                                q.shape[1])
             state["step"] = step
             self._update_dispatch(state)
             self.phase_counts["exact_refresh"] += 1

@@ -130,9 +130,14 @@ def sampled_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128, sampl
 
 
 def exact_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128,
-                     scale: float | None = None) -> torch.Tensor:
-    """Exact dense block mass ``[B, H, Qb, Qb]`` (reference ``flex.py:97-108,167-202``)."""
-    device = _require_cuda(q, k)
+                     scale: float | None = None, lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact dense block mass ``[B, H, Qb, Qb]`` (reference ``flex.py:97-108,167-202``).
+
+    ``lse``: fp32 ``[B, H, T]`` natural-log log-sum-exp of each query row (the
+    dense pass's, as the reference passes it); without it the kernel computes
+    it in a first pass.
+    """
+    device = _require_cuda(q, k, lse)
     if q.shape != k.shape or q.dim() != 4:
         raise ValueError("q and k must be [B, T, H, D] with equal shapes")
     q = q.to(torch.bfloat16).contiguous()
@@ -141,10 +146,15 @@ def exact_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128,
     if D != HEAD_DIM:
         raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
     blocks = math.ceil(T / block)
+    if lse is not None:
+        if tuple(lse.shape) != (B, H, T):
+            raise ValueError(f"lse must be [B, H, T] = {(B, H, T)}")
+        lse = lse.to(torch.float32).contiguous()
     mass = torch.empty((B, H, blocks, blocks), dtype=torch.float32, device=device)
     s = float(scale) if scale is not None else D ** -0.5
     _native.call("bsa_exact_block_mass", q.data_ptr(), k.data_ptr(), B, T, H, D, block, s,
-                 mass.data_ptr(), _native.err_word(device).data_ptr(), _stream(device))
+                 _native.ptr(lse), mass.data_ptr(), _native.err_word(device).data_ptr(),
+                 _stream(device))
     return mass
 
 

@@ -191,13 +191,16 @@ BSA_API int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch
  *   mass[b, h, qb, kb] = sum_{q in qb, k in kb, q,k < tokens} softmax_q(k)
  * over full-precision scores (no bf16 rounding) of q, k: bf16 [batch, tokens,
  * heads, head_dim] contiguous.  Writes fp32 [batch, heads, Qb, Qb].
- * block in {32, 64, 128}, head_dim == 128, Qb <= 4096.
+ * block in {32, 64, 128}, head_dim == 128, Qb <= 4096.  lse: fp32 [batch,
+ * heads, tokens], the natural-log log-sum-exp of each query row's scaled
+ * scores (for example from bsa_attention_fwd over a full route), or NULL: then
+ * the kernel computes it in a first pass over the keys.
  * Replaces: attention_backends/flex.py:97-108,167-202 (_block_attention_mass,
  *           given the LSE of the dense FlexAttention pass of flex.py:254-272).
  */
 BSA_API int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t tokens,
-                         int64_t heads, int32_t head_dim, int32_t block, float scale, float* mass,
-                         int32_t* err_word, void* stream);
+                         int64_t heads, int32_t head_dim, int32_t block, float scale,
+                         const float* lse, float* mass, int32_t* err_word, void* stream);
 
 /*
  * (a) Block-sparse attention forward.

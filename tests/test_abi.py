@@ -86,7 +86,7 @@ def test_attention_and_mass_validate():
     assert "head_dim" in _err()
     assert lib.bsa_sampled_mass(16, 16, 1, 1, 4, 3, 128, 16, 0.1, 1, 16, 16, None) == -2
     assert "samples" in _err()
-    assert lib.bsa_exact_block_mass(16, 16, 1, 100, 1, 128, 96, 0.1, 16, 16, None) == -2
+    assert lib.bsa_exact_block_mass(16, 16, 1, 100, 1, 128, 96, 0.1, None, 16, 16, None) == -2
     assert "block" in _err()
 
 

@@ -237,3 +237,59 @@ def test_sampled_full_equals_exact_over_block():
     np.testing.assert_allclose(sampled.cpu().numpy(), exact.cpu().numpy() / 32, rtol=1e-4,
                                atol=1e-7)
     np.testing.assert_allclose(exact.sum(-1).cpu().numpy(), 32.0, rtol=1e-3)
+
+
+def _exact_reference(q, k, block):
+    """float64 oracle mass and LSE of bf16 ``q, k [1, T, H, D]``."""
+    qf, kf = q[0].double().cpu().numpy(), k[0].double().cpu().numpy()
+    scores = np.einsum("qhd,khd->hqk", qf, kf) * 128 ** -0.5
+    mx = scores.max(-1, keepdims=True)
+    lse = (mx + np.log(np.exp(scores - mx).sum(-1, keepdims=True)))[..., 0]
+    return oroute.exact_block_mass(qf, kf, lse, block), lse
+
+
+@pytest.mark.parametrize("tokens,heads,block", [
+    (5000, 2, 128),     # 40 key tiles: three groups of the cross-warp reduction, partial tail
+    (1000, 3, 64),      # 64-token blocks: two query and two key blocks per tile
+    (4096, 1, 128),     # exactly two full groups
+])
+def test_exact_mass_wide_blocks_match_oracle_and_repeat(tokens, heads, block):
+    g = torch.Generator().manual_seed(tokens + heads)
+    q = torch.randn((1, tokens, heads, 128), generator=g).to(torch.bfloat16)
+    k = torch.randn((1, tokens, heads, 128), generator=g).to(torch.bfloat16)
+    ref, lse = _exact_reference(q, k, block)
+    qd, kd = q.to(DEV), k.to(DEV)
+    first = kernels.exact_block_mass(qd, kd, block)
+    second = kernels.exact_block_mass(qd, kd, block)
+    given = kernels.exact_block_mass(qd, kd, block,
+                                     lse=torch.from_numpy(lse).float().unsqueeze(0).to(DEV))
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.equal(first, second)                       # deterministic reduction order
+    np.testing.assert_allclose(first[0].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
+    np.testing.assert_allclose(given[0].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
+    torch.testing.assert_close(given, first, atol=1e-4, rtol=1e-4)
+    rows = np.minimum(block, tokens - np.arange(ref.shape[1]) * block)
+    np.testing.assert_allclose(first[0].sum(-1).cpu().numpy(),
+                               np.broadcast_to(rows, ref.shape[:2]), rtol=1e-3)
+
+
+def test_exact_mass_from_attention_lse_batch2():
+    """The bootstrap's pairing: LSE of the routed attention over a full route,
+    then one mass pass; batch 2 with a partial tail."""
+    g = torch.Generator().manual_seed(3)
+    B, T, H = 2, 1500, 2
+    q, k, v = (torch.randn((B, T, H, 128), generator=g).to(torch.bfloat16).to(DEV)
+               for _ in range(3))
+    blocks = math.ceil(T / 128)
+    full = torch.ones((B, H, blocks, blocks), dtype=torch.bool, device=DEV)
+    counts, indices = kernels.pack_boolean_rows(full)
+    _, lse = kernels.block_sparse_attention(q, k, v, counts, indices, 128, return_lse=True)
+    mass = kernels.exact_block_mass(q, k, 128, lse=lse)
+    two_pass = kernels.exact_block_mass(q, k, 128)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    torch.testing.assert_close(mass, two_pass, atol=1e-4, rtol=1e-3)
+    for b in range(B):
+        ref, _ = _exact_reference(q[b:b + 1].cpu(), k[b:b + 1].cpu(), 128)
+        np.testing.assert_allclose(mass[b].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
