@@ -532,27 +532,20 @@ def route_stage(cfg, qp, kp, route, kernels, device, stream, neighbors):
 
 
 def bootstrap_stage(cfg, qp, kp, vp, kernels, stream):
-    """Exact bootstrap of this layer (flex.py:254-272): dense attention over all
-    blocks with its LSE, then the exact block mass from that LSE."""
+    """Exact bootstrap of this layer (flex.py:254-272): dense attention that
+    also yields its exact block mass (one pass over the keys)."""
     from dit_sparse_atten_b200 import _native
-    from dit_sparse_atten_b200.flex import _dense_with_lse
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    for i in range(2):
-        if i == 1:
-            ev[0].record(stream)
-        _, lse = _dense_with_lse(qp, kp, vp, cfg.block)
-        if i == 1:
-            ev[1].record(stream)
-        kernels.exact_block_mass(qp, kp, cfg.block, lse=lse)
-    ev[2].record(stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    kernels.dense_attention_block_mass(qp, kp, vp)
+    ev[0].record(stream)
+    kernels.dense_attention_block_mass(qp, kp, vp)
+    ev[1].record(stream)
     torch.cuda.synchronize()
     _native.check_device_errors()
-    dense_ms, mass_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    ms = ev[0].elapsed_time(ev[1])
     B, T, H, D = qp.shape
-    exps = B * H * T * T
-    return {"bootstrap_dense_ms": dense_ms, "bootstrap_exact_mass_ms": mass_ms,
-            "bootstrap_dense_tflops": 4.0 * B * H * T * T * D / dense_ms / 1e9,
-            "bootstrap_exact_mass_gexp_per_s": exps / mass_ms / 1e6}
+    return {"bootstrap_dense_and_mass_ms": ms,
+            "bootstrap_dense_tflops": 4.0 * B * H * T * T * D / ms / 1e9}
 
 
 def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total_flops):

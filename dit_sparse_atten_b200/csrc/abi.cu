@@ -438,12 +438,13 @@ int bsa_exact_block_mass(const void* q, const void* k, int64_t batch, int64_t to
   return ok();
 }
 
-int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
-                      int64_t heads, int32_t head_dim, int64_t in_stride_b, int64_t in_stride_t,
-                      int64_t in_stride_h, const int32_t* counts, const int32_t* indices,
-                      int32_t route_cols, int32_t route_has_batch, int32_t block, float scale,
-                      void* out, int64_t out_stride_b, int64_t out_stride_t,
-                      int64_t out_stride_h, float* lse, int32_t* err_word, void* stream) {
+static int attention_launch(const char* name, const void* q, const void* k, const void* v,
+                            int64_t batch, int64_t tokens, int64_t heads, int32_t head_dim,
+                            int64_t in_stride_b, int64_t in_stride_t, int64_t in_stride_h,
+                            const int32_t* counts, const int32_t* indices, int32_t route_cols,
+                            int32_t route_has_batch, int32_t block, float scale, void* out,
+                            int64_t out_stride_b, int64_t out_stride_t, int64_t out_stride_h,
+                            float* lse, float* block_lse, int32_t* err_word, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || counts == nullptr ||
       indices == nullptr || err_word == nullptr)
     return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
@@ -494,8 +495,48 @@ int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
   a.out_stride_h = out_stride_h;
   a.lse = lse;
   a.err_word = err_word;
+  a.block_lse = block_lse;
   cudaError_t e = bsa::launch_attention(tq, tk, tv, a, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "bsa_attention_fwd launch");
+  if (e != cudaSuccess) return cuda_fail(e, name);
+  return ok();
+}
+
+int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch, int64_t tokens,
+                      int64_t heads, int32_t head_dim, int64_t in_stride_b, int64_t in_stride_t,
+                      int64_t in_stride_h, const int32_t* counts, const int32_t* indices,
+                      int32_t route_cols, int32_t route_has_batch, int32_t block, float scale,
+                      void* out, int64_t out_stride_b, int64_t out_stride_t,
+                      int64_t out_stride_h, float* lse, int32_t* err_word, void* stream) {
+  return attention_launch("bsa_attention_fwd launch", q, k, v, batch, tokens, heads, head_dim,
+                          in_stride_b, in_stride_t, in_stride_h, counts, indices, route_cols,
+                          route_has_batch, block, scale, out, out_stride_b, out_stride_t,
+                          out_stride_h, lse, nullptr, err_word, stream);
+}
+
+int bsa_attention_dense_block_mass(const void* q, const void* k, const void* v, int64_t batch,
+                                   int64_t tokens, int64_t heads, int32_t head_dim,
+                                   int64_t in_stride_b, int64_t in_stride_t, int64_t in_stride_h,
+                                   float scale, void* out, int64_t out_stride_b,
+                                   int64_t out_stride_t, int64_t out_stride_h, float* lse,
+                                   float* block_lse, float* mass, int32_t* err_word,
+                                   void* stream) {
+  if (lse == nullptr || block_lse == nullptr || mass == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "lse, block_lse and mass must not be null");
+  const int64_t blocks = (tokens + 127) / 128;
+  if (blocks > 4096) return fail(BSA_ERR_UNSUPPORTED, "at most 4096 blocks");
+  // The dense instantiation reads no route; counts / indices only satisfy
+  // the shared argument checks.
+  static const int32_t kNoRoute[1] = {0};
+  int rc = attention_launch("bsa_attention_dense_block_mass launch", q, k, v, batch, tokens,
+                            heads, head_dim, in_stride_b, in_stride_t, in_stride_h, kNoRoute,
+                            kNoRoute, static_cast<int32_t>(blocks), 0, 128, scale, out,
+                            out_stride_b, out_stride_t, out_stride_h, lse, block_lse, err_word,
+                            stream);
+  if (rc != BSA_OK) return rc;
+  cudaError_t e = bsa::launch_block_mass(block_lse, lse, batch, tokens, heads,
+                                         static_cast<int32_t>(blocks), mass,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_attention_dense_block_mass mass launch");
   return ok();
 }
 

@@ -213,7 +213,12 @@ __device__ __forceinline__ float2 row_exp(uint32_t sbuf, bool partial, int64_t v
   return __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
 }
 
-template <int BK>
+// kDenseMass: every key block in order (no CSR), and each query row also
+// writes, per key block kb, v = log2 of its exponential sum over the block's
+// keys (the online softmax's block row sum, shifted back by the stabiliser it
+// used) to a.block_lse[b, h, kb, row]; block_mass_kernel turns these and the
+// row LSE into the exact block mass.
+template <int BK, bool kDenseMass>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     bsa_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -236,8 +241,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int b = blockIdx.z;
   const int64_t rb = a.route_batch_stride ? b : 0;
   const int64_t route_row = (rb * a.heads + h) * a.q_blocks + qb;
-  const int32_t* kv_list = a.indices + route_row * a.route_cols;
-  int n = a.counts[route_row];
+  const int32_t* kv_list = kDenseMass ? nullptr : a.indices + route_row * a.route_cols;
+  int n = kDenseMass ? a.k_blocks : a.counts[route_row];
   if (n < 0 || n > a.route_cols || n > a.k_blocks) {
     if (threadIdx.x == 0) atomicOr(a.err_word, kErrBadRoute);
     n = n < 0 ? 0 : min(n, min(a.route_cols, a.k_blocks));
@@ -284,6 +289,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = bar->tmem_base;
 
   auto block_id = [&](int j) -> int {
+    if constexpr (kDenseMass) return j;
     int kb = __ldg(kv_list + j);
     if (kb < 0 || kb >= a.k_blocks) {
       atomicOr(a.err_word, kErrBadRoute);
@@ -446,6 +452,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float2 rs = partial ? row_exp<BK, 0>(sbuf, true, valid, c2, neg_m, keep)
                                   : row_exp<BK, kEmulatedPairsPer8>(sbuf, false, valid, c2, neg_m, keep);
         l += rs.x + rs.y;
+        if constexpr (kDenseMass) {
+          if (row_valid) {
+            float* dst = a.block_lse + static_cast<int64_t>(kb) * a.tokens + token;
+            dst[(static_cast<int64_t>(b) * a.heads + h) * a.k_blocks * a.tokens] =
+                m_used + __log2f(rs.x + rs.y);
+          }
+        }
       }
       // O holds the blocks before j relative to m_prev: a moved stabiliser
       // rescales it once PV_{j-1} is done (rare after the first blocks).
@@ -537,7 +550,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
-template <int BK>
+template <int BK, bool kDenseMass>
 cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                       const AttnArgs& a, cudaStream_t stream) {
   using L = AttnLayout<BK>;
@@ -554,24 +567,71 @@ cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
     if (e != cudaSuccess) return e;
     bytes = optin < L::kUsed + 1024 ? optin : L::kUsed + 1024;
     if (bytes < L::kUsed) return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(bsa_attention_kernel<BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             bytes);
+    e = cudaFuncSetAttribute(bsa_attention_kernel<BK, kDenseMass>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) smem_bytes[dev] = bytes;
   }
   const dim3 grid(static_cast<unsigned>(a.q_blocks), static_cast<unsigned>(a.heads),
                   static_cast<unsigned>(a.batch));
-  bsa_attention_kernel<BK><<<grid, kAttnThreads, bytes, stream>>>(tq, tk, tv, a);
+  bsa_attention_kernel<BK, kDenseMass><<<grid, kAttnThreads, bytes, stream>>>(tq, tk, tv, a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
+namespace {
+
+// mass[b, h, qb, kb] = sum over the rows r < T of query block qb of
+// 2^(block_lse[b, h, kb, r] - lse[b, h, r] * log2(e)): one warp per
+// (query block, key block) cell, rows added in a fixed order.
+__global__ void __launch_bounds__(256) block_mass_kernel(const float* __restrict__ block_lse,
+                                                         const float* __restrict__ lse,
+                                                         int64_t tokens, int heads, int blocks,
+                                                         float* __restrict__ mass) {
+  const int kb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t bh = static_cast<int64_t>(b) * heads + h;
+  const float* v = block_lse + (bh * blocks + kb) * tokens;
+  const float* l = lse + bh * tokens;
+  for (int qb = warp; qb < blocks; qb += 8) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t r = static_cast<int64_t>(qb) * 128 + i * 32 + lane;
+      if (r < tokens) acc += ex2_approx(__ldg(v + r) - __ldg(l + r) * kLog2e);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) mass[(bh * blocks + qb) * blocks + kb] = acc;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_block_mass(const float* block_lse, const float* lse, int64_t batch,
+                              int64_t tokens, int64_t heads, int32_t blocks, float* mass,
+                              cudaStream_t stream) {
+  if (batch == 0 || heads == 0 || blocks == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(heads),
+                  static_cast<unsigned>(batch));
+  block_mass_kernel<<<grid, 256, 0, stream>>>(block_lse, lse, tokens, static_cast<int>(heads),
+                                              blocks, mass);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnArgs& a, cudaStream_t stream) {
   if (a.batch == 0 || a.heads == 0 || a.q_blocks == 0) return cudaSuccess;
-  if (a.block == 128) return launch_bk<128>(tq, tk, tv, a, stream);
-  if (a.block == 64) return launch_bk<64>(tq, tk, tv, a, stream);
+  if (a.block_lse != nullptr) {
+    if (a.block == 128) return launch_bk<128, true>(tq, tk, tv, a, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (a.block == 128) return launch_bk<128, false>(tq, tk, tv, a, stream);
+  if (a.block == 64) return launch_bk<64, false>(tq, tk, tv, a, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -115,10 +115,19 @@ struct AttnArgs {
   int64_t out_stride_b, out_stride_t, out_stride_h;
   float* lse;                     // [B, H, T] or nullptr
   int* err_word;
+  // Dense attention with block mass: non-null selects every key block in
+  // order (counts / indices unused) and receives [B, H, Kb, T] per-row,
+  // per-key-block log2 exponential sums (block == 128).
+  float* block_lse;
 };
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args,
                              cudaStream_t stream);
+// mass [B, H, Kb, Kb] from block_lse [B, H, Kb, T] and the natural-log row LSE
+// [B, H, T] of the same dense pass (128-token blocks).
+cudaError_t launch_block_mass(const float* block_lse, const float* lse, int64_t batch,
+                              int64_t tokens, int64_t heads, int32_t blocks, float* mass,
+                              cudaStream_t stream);
 
 // ---- diagnostics ------------------------------------------------------------
 cudaError_t launch_exp2(const float* x, float* y, int64_t n, int mode, cudaStream_t stream);

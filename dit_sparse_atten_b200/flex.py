@@ -135,42 +135,30 @@ def _flex_output(q, k, v, block_mask, block_size, compile_kernel=True, scale=Non
     return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size, scale=scale)
 
 
-_FULL_ROUTES = {}
-
-
-def _full_route(heads, blocks, device):
-    """CSR of the all-blocks route ``[H, Qb]`` / ``[H, Qb, Qb]`` (cached)."""
-    key = (heads, blocks, torch.device(device))
-    if key not in _FULL_ROUTES:
-        if len(_FULL_ROUTES) > 8:
-            _FULL_ROUTES.clear()
-        _FULL_ROUTES[key] = kernels.pack_boolean_rows(
-            torch.ones((heads, blocks, blocks), dtype=torch.bool, device=device))
-    return _FULL_ROUTES[key]
-
-
-def _dense_with_lse(q, k, v, block_size, scale=None):
-    """Dense attention and its per-query log-sum-exp ``[1, H, T]`` in one kernel:
-    the routed attention over the all-blocks route (the reference's dense
-    FlexAttention call with ``return_lse=True``, ``flex.py:260-265``).  Returns
-    ``(None, None)`` for inputs the kernel does not take (not bf16 / D != 128)."""
-    if q.dtype != torch.bfloat16 or q.shape[-1] != kernels.HEAD_DIM or not q.is_cuda:
+def _dense_and_mass(q, k, v, block_size, scale=None):
+    """Dense output and exact block mass ``[1, H, Qb, Qb]`` from one attention
+    pass (the reference's dense FlexAttention with ``return_lse`` followed by
+    ``_block_attention_mass``, ``flex.py:254-272``).  ``(None, None)`` for
+    inputs that kernel does not take (not CUDA bf16, D != 128, block != 128)."""
+    if (q.dtype != torch.bfloat16 or q.shape[-1] != kernels.HEAD_DIM or not q.is_cuda
+            or block_size != 128):
         return None, None
-    counts, indices = _full_route(q.shape[2], math.ceil(q.shape[1] / block_size), q.device)
-    return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size,
-                                          scale=scale, return_lse=True)
+    out, _, mass = kernels.dense_attention_block_mass(q, k, v, scale=scale)
+    return out, mass
 
 
 def _dense_bootstrap(q, k, v, block_size, mass_target, keep, compile_kernel, scale=None):
-    """Dense output and its exact block top-mass route (``flex.py:254-272``):
-    one attention pass that also returns the LSE, then one mass pass."""
+    """Dense output and its exact block top-mass route (``flex.py:254-272``),
+    from one attention pass that also yields the block mass."""
     if q.shape[0] != 1 or q.shape[1] != k.shape[1]:
         raise ValueError("Flex bootstrap supports batch-1 self-attention")
     del compile_kernel
-    output, lse = _dense_with_lse(q, k, v, block_size, scale)
+    output, mass = _dense_and_mass(q, k, v, block_size, scale)
     if output is None:
         output = DenseBackend()(q, k, v, softmax_scale=scale, dtype=q.dtype)
-    mass = _block_attention_mass(q, k, lse, block_size, scale=scale)
+        mass = _block_attention_mass(q, k, None, block_size, scale=scale)
+    else:
+        mass = mass[0]
     return output, _top_mass_route(mass, mass_target, keep)
 
 
@@ -368,17 +356,18 @@ class FlexReuseBackend:
         return result
 
     def _dense_for_exact_route(self, q, k, v, softmax_scale, dense_only):
-        """Dense output plus the LSE the exact mass pass reuses (one attention
-        kernel over the all-blocks route), or SDPA and no LSE for inputs that
-        kernel does not take."""
-        output, lse = _dense_with_lse(q, k, v, self.config.block_size, softmax_scale)
+        """Dense output plus its exact block mass from one attention pass, or
+        SDPA and no mass (computed later from q, k) for inputs that kernel
+        does not take."""
+        output, mass = _dense_and_mass(q, k, v, self.config.block_size, softmax_scale)
         if output is None:
             return self.dense(q, k, v, **dense_only), None
-        return output, lse
+        return output, mass[0]
 
-    def _exact_route(self, state, q, k, softmax_scale, lse=None):
+    def _exact_route(self, state, q, k, softmax_scale, mass=None):
         c = self.config
-        mass = _block_attention_mass(q, k, lse, c.block_size, scale=softmax_scale)
+        if mass is None:
+            mass = _block_attention_mass(q, k, None, c.block_size, scale=softmax_scale)
         result = kernels.route_select(mass, target=c.mass_target, keep=c.keep,
                                       sink_blocks=self._sink_blocks(state))
         return self._result_from_csr(state, result, q.shape[1])
@@ -513,9 +502,9 @@ class FlexReuseBackend:
             state = {"route": None, "frontier": None, "block_mask": None, "step": step,
                      "layout": layout, "grid": grid}
             if self.config.bootstrap_mode == "exact":
-                output, lse = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
+                output, mass = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
                 self.state[key] = state
-                self._install_route(state, self._exact_route(state, q, k, softmax_scale, lse),
+                self._install_route(state, self._exact_route(state, q, k, softmax_scale, mass),
                                     q.shape[1])
                 self._update_dispatch(state)
                 self.phase_counts["dense_bootstrap"] += 1
@@ -547,8 +536,8 @@ class FlexReuseBackend:
         if (self.config.update_interval > 0
                 and (step - state["step"]) >= self.config.update_interval
                 and not self._is_final_step(step)):
-            output, lse = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
-            self._install_route(state, self._exact_route(state, q, k, softmax_scale, lse),
+            output, mass = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
+            self._install_route(state, self._exact_route(state, q, k, softmax_scale, mass),
                                 q.shape[1])
             state["step"] = step
             self._update_dispatch(state)

@@ -329,6 +329,51 @@ def directional_update(mass: torch.Tensor, previous: torch.Tensor, neighbors: to
 # (a) attention
 # ----------------------------------------------------------------------------
 
+def dense_attention_block_mass(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                               scale: float | None = None,
+                               workspace_bytes: int = 2 << 30):
+    """Dense attention, its LSE and its exact block mass in one attention pass.
+
+    ``q, k, v``: bf16 ``[B, T, H, 128]``.  Returns ``out`` bf16 ``[B, T, H, D]``,
+    ``lse`` fp32 ``[B, H, T]`` (natural log) and ``mass`` fp32 ``[B, H, Qb, Qb]``
+    over 128-token blocks: the reference's dense bootstrap (``flex.py:254-272``:
+    FlexAttention with ``return_lse`` then ``_block_attention_mass``) without
+    the second pass over the keys.  Heads go in chunks whose per-row block
+    sums fit ``workspace_bytes``.
+    """
+    device = _require_cuda(q, k, v)
+    if not (q.shape == k.shape == v.shape) or q.dim() != 4:
+        raise ValueError("q, k and v must be [B, T, H, D] with equal shapes")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("dense_attention_block_mass expects bf16 q, k, v")
+    B, T, H, D = q.shape
+    if D != HEAD_DIM:
+        raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    blocks = math.ceil(T / 128)
+    out = torch.empty_like(q)
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=device)
+    mass = torch.empty((B, H, blocks, blocks), dtype=torch.float32, device=device)
+    per_head = blocks * T * 4
+    hc = max(1, min(H, workspace_bytes // per_head))
+    work = torch.empty((hc, blocks, T), dtype=torch.float32, device=device)
+    s = float(scale) if scale is not None else D ** -0.5
+    st, ost = q.stride(), out.stride()
+    esz = q.element_size()
+    for b in range(B):
+        for h0 in range(0, H, hc):
+            n = min(hc, H - h0)
+            off = (b * st[0] + h0 * st[2]) * esz
+            ooff = (b * ost[0] + h0 * ost[2]) * esz
+            _native.call("bsa_attention_dense_block_mass", q.data_ptr() + off,
+                         k.data_ptr() + off, v.data_ptr() + off, 1, T, n, D, st[0], st[1], st[2],
+                         s, out.data_ptr() + ooff, ost[0], ost[1], ost[2],
+                         lse[b, h0:h0 + n].data_ptr(), work.data_ptr(),
+                         mass[b, h0:h0 + n].data_ptr(), _native.err_word(device).data_ptr(),
+                         _stream(device))
+    return out, lse, mass
+
+
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            counts: torch.Tensor, indices: torch.Tensor, block: int = 128,
                            scale: float | None = None, out: torch.Tensor | None = None,

@@ -230,6 +230,28 @@ BSA_API int bsa_attention_fwd(const void* q, const void* k, const void* v, int64
  * degree-3, relative error <= 1e-4 for x >= -126).  No reference
  * counterpart: it exists so the approximation can be tested on its own.
  */
+/*
+ * (a) + (f1) Dense attention with its exact block mass, one attention pass:
+ * out = softmax(q k^T * scale) v over all keys, lse = its natural-log
+ * log-sum-exp per query row ([batch, heads, tokens]), and
+ *   mass[b, h, qb, kb] = sum_{q in qb, k in kb} softmax_q(k)
+ * ([batch, heads, Qb, Qb], 128-token blocks) as bsa_exact_block_mass with that
+ * lse, without a second pass over the keys: the attention writes, per query
+ * row and key block, the log2 of the block's exponential sum to block_lse
+ * (fp32 workspace [batch, heads, Qb, tokens], contents on return unspecified)
+ * and a reduction kernel normalises and sums them.  Inputs and out as
+ * bsa_attention_fwd (head_dim 128); Qb <= 4096.
+ * Replaces: attention_backends/flex.py:254-272 (_dense_bootstrap: dense
+ *           FlexAttention with return_lse, then _block_attention_mass).
+ */
+BSA_API int bsa_attention_dense_block_mass(const void* q, const void* k, const void* v,
+                                           int64_t batch, int64_t tokens, int64_t heads,
+                                           int32_t head_dim, int64_t in_stride_b,
+                                           int64_t in_stride_t, int64_t in_stride_h, float scale,
+                                           void* out, int64_t out_stride_b, int64_t out_stride_t,
+                                           int64_t out_stride_h, float* lse, float* block_lse,
+                                           float* mass, int32_t* err_word, void* stream);
+
 BSA_API int bsa_exp2(const float* x, float* y, int64_t n, int32_t mode, void* stream);
 
 #ifdef __cplusplus

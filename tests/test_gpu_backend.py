@@ -107,9 +107,9 @@ def test_exact_bootstrap_route(monkeypatch):
     out = backend(q, k, v)
     close(out, sdpa(q, k, v))
     state = next(iter(backend.state.values()))
-    # the bootstrap's pairing: LSE of the attention over all blocks, one mass pass
-    _, lse = flex_module._dense_with_lse(q, k, v, 128)
-    mass = kernels.exact_block_mass(q, k, 128, lse=lse)[0].cpu().numpy()
+    # the bootstrap's mass: from the same dense attention pass
+    _, _, mass = kernels.dense_attention_block_mass(q, k, v)
+    mass = mass[0].cpu().numpy()
     expect = oroute.sampled_route(mass, None, 0.0, 0.9, 0.5, grid=(2, 16, 32), block=128)
     np.testing.assert_array_equal(state["route"].cpu().numpy(), expect)
     assert backend.phase_counts["dense_bootstrap"] == 1

@@ -293,3 +293,28 @@ def test_exact_mass_from_attention_lse_batch2():
     for b in range(B):
         ref, _ = _exact_reference(q[b:b + 1].cpu(), k[b:b + 1].cpu(), 128)
         np.testing.assert_allclose(mass[b].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("B,T,H,workspace", [(2, 1500, 3, 2 << 30), (1, 2200, 4, 1)])
+def test_dense_attention_block_mass(B, T, H, workspace):
+    """One dense pass gives the output and LSE of the all-blocks routed
+    attention (bit for bit) and the exact block mass; a tiny workspace forces
+    one head per launch."""
+    g = torch.Generator().manual_seed(T + H)
+    q, k, v = (torch.randn((B, T, H, 128), generator=g).to(torch.bfloat16).to(DEV)
+               for _ in range(3))
+    out, lse, mass = kernels.dense_attention_block_mass(q, k, v, workspace_bytes=workspace)
+    blocks = math.ceil(T / 128)
+    full = torch.ones((B, H, blocks, blocks), dtype=torch.bool, device=DEV)
+    counts, indices = kernels.pack_boolean_rows(full)
+    ref_out, ref_lse = kernels.block_sparse_attention(q, k, v, counts, indices, 128,
+                                                      return_lse=True)
+    two_pass = kernels.exact_block_mass(q, k, 128)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16))
+    assert torch.equal(lse, ref_lse)
+    torch.testing.assert_close(mass, two_pass, atol=2e-5, rtol=1e-4)
+    for b in range(B):
+        ref, _ = _exact_reference(q[b:b + 1].cpu(), k[b:b + 1].cpu(), 128)
+        np.testing.assert_allclose(mass[b].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
