@@ -25,6 +25,8 @@ SIGNATURES = {
     "bsa_pack_boolean_rows": ([_P, _I64, _I32, _P, _P, _P], _I32),
     "bsa_route_select": ([_P, _P, _I64, _I32, _I32, _F32, _F32, _I32, _I32, _P, _P, _P, _P, _P],
                          _I32),
+    "bsa_qkv_prologue": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I32, _I32, _P, _P,
+                          _F32, _P, _P, _P, _P, _P, _P, _P, _P], _I32),
     "bsa_frontier_mask": ([_P, _P, _I64, _I32, _P, _P, _P], _I32),
     "bsa_directional_update": ([_P, _P, _P, _P, _I64, _I32, _F32, _F32, _F32, _F32, _I32, _I32,
                                 _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

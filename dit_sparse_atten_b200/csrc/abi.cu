@@ -183,6 +183,53 @@ int bsa_route_select(const float* mass, const uint8_t* prev, int64_t rows, int32
   return ok();
 }
 
+int bsa_qkv_prologue(const void* q_proj, const void* k_proj, const void* v_proj, int64_t batch,
+                     int64_t tokens, int64_t heads, int32_t head_dim, int64_t in_stride_b,
+                     int64_t in_stride_t, int32_t norm_q, int32_t norm_k,
+                     const float* norm_q_weight, const float* norm_k_weight, float eps,
+                     const float* rope_cos, const float* rope_sin, const int32_t* perm,
+                     void* q_out, void* k_out, void* v_out, int32_t* err_word, void* stream) {
+  if (q_proj == nullptr || k_proj == nullptr || v_proj == nullptr || q_out == nullptr ||
+      k_out == nullptr || v_out == nullptr || err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (batch < 0 || tokens < 0 || heads <= 0 || head_dim <= 0 || head_dim % 8 != 0 ||
+      heads * head_dim > (1 << 20))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/tokens/heads/head_dim (head_dim %% 8 == 0)");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(BSA_ERR_INVALID_ARGUMENT, "rope_cos and rope_sin go together");
+  const void* ptrs[] = {q_proj, k_proj, v_proj, q_out, k_out, v_out, rope_cos, rope_sin};
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15)
+      return fail(BSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+  if ((in_stride_b * 2) % 16 || (in_stride_t * 2) % 16)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "row strides must be multiples of 8 elements");
+  bsa::PrologueArgs a{};
+  a.q_in = static_cast<const __nv_bfloat16*>(q_proj);
+  a.k_in = static_cast<const __nv_bfloat16*>(k_proj);
+  a.v_in = static_cast<const __nv_bfloat16*>(v_proj);
+  a.batch = batch;
+  a.tokens = tokens;
+  a.heads = static_cast<int32_t>(heads);
+  a.head_dim = head_dim;
+  a.in_stride_b = in_stride_b;
+  a.in_stride_t = in_stride_t;
+  a.norm_q = norm_q != 0;
+  a.norm_k = norm_k != 0;
+  a.weight_q = norm_q_weight;
+  a.weight_k = norm_k_weight;
+  a.eps = eps;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.perm = perm;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_out = static_cast<__nv_bfloat16*>(k_out);
+  a.v_out = static_cast<__nv_bfloat16*>(v_out);
+  a.err_word = err_word;
+  cudaError_t e = bsa::launch_qkv_prologue(a, static_cast<cudaStream_t>(stream), sm_count());
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_qkv_prologue launch");
+  return ok();
+}
+
 int bsa_frontier_mask(const uint8_t* route, const int32_t* neighbors, int64_t planes,
                       int32_t blocks, uint8_t* frontier, int32_t* err_word, void* stream) {
   if (route == nullptr || neighbors == nullptr || frontier == nullptr)

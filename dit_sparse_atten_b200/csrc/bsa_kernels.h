@@ -35,6 +35,28 @@ struct SelectArgs {
 };
 cudaError_t launch_route_select(const SelectArgs& args, cudaStream_t stream);
 
+// ---- (f4) attention prologue ------------------------------------------------
+struct PrologueArgs {
+  const __nv_bfloat16* q_in;      // [B, T, H * D] projections, row strides below (elements)
+  const __nv_bfloat16* k_in;
+  const __nv_bfloat16* v_in;
+  int64_t batch, tokens;
+  int32_t heads, head_dim;
+  int64_t in_stride_b, in_stride_t;
+  bool norm_q, norm_k;            // RMSNorm of Q / K over H * D
+  const float* weight_q;          // [H * D] or nullptr (no affine)
+  const float* weight_k;
+  float eps;
+  const float* rope_cos;          // [T, D / 2] or nullptr (no rotary embedding)
+  const float* rope_sin;
+  const int32_t* perm;            // [T] output row -> input token, or nullptr
+  __nv_bfloat16* q_out;           // [B, T, H, D] contiguous, packed order
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;
+  int* err_word;
+};
+cudaError_t launch_qkv_prologue(const PrologueArgs& args, cudaStream_t stream, int num_sms);
+
 // ---- (f3) directional frontier update ---------------------------------------
 enum DirectionalExpand : int { kExpandQ = 1, kExpandK = 2, kExpandJoint = 4 };
 

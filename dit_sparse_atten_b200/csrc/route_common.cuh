@@ -24,16 +24,16 @@ __device__ __forceinline__ int ceil_log2(int v) {
   return v <= 1 ? 0 : 32 - __clz(v - 1);
 }
 
-// Cascade over `size` items; item i of this lane is x[index(i)].
-template <typename IndexFn>
-__device__ float cascade_sum(const float* x, int size, IndexFn index) {
+// Cascade over `size` items; item i of this lane is load(index(i)).
+template <typename Load, typename IndexFn>
+__device__ float cascade_sum(Load load, int size, IndexFn index) {
   const int level_power = max(4, ceil_log2(size) / 4);
   const int level_step = 1 << level_power;
   const int level_mask = level_step - 1;
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
   int i = 0;
   while (i + level_step <= size) {
-    for (int j = 0; j < level_step; ++j, ++i) acc0 = __fadd_rn(acc0, x[index(i)]);
+    for (int j = 0; j < level_step; ++j, ++i) acc0 = __fadd_rn(acc0, load(index(i)));
     acc1 = __fadd_rn(acc1, acc0);
     acc0 = 0.f;
     if ((i & (level_mask << level_power)) != 0) continue;
@@ -43,25 +43,30 @@ __device__ float cascade_sum(const float* x, int size, IndexFn index) {
     acc3 = __fadd_rn(acc3, acc2);
     acc2 = 0.f;
   }
-  for (; i < size; ++i) acc0 = __fadd_rn(acc0, x[index(i)]);
+  for (; i < size; ++i) acc0 = __fadd_rn(acc0, load(index(i)));
   acc0 = __fadd_rn(acc0, acc1);
   acc0 = __fadd_rn(acc0, acc2);
   acc0 = __fadd_rn(acc0, acc3);
   return acc0;
 }
 
-// float32 row sum in the reference's CPU order; executed by one full warp,
-// result valid in every lane.
-__device__ float torch_cpu_row_sum(const float* x, int n) {
+// float32 sum of load(0..n-1) in the reference's CPU order (ATen's vectorised
+// cascade: lane (k, v) of 4 accumulators x 8 float lanes takes items
+// (4 i + k) * 8 + v, i.e. warp lane k * 8 + v takes items 32 i + lane);
+// executed by one full warp, result valid in every lane.
+template <typename Load>
+__device__ float torch_cpu_sum(Load load, int n) {
   const int lane = threadIdx.x & 31;
   float result = 0.f;
   if (n < 8) {
     if (lane == 0) {
       const int size_ilp = n / 4;
       float p[4];
+#pragma unroll
       for (int k = 0; k < 4; ++k)
-        p[k] = cascade_sum(x, size_ilp, [k](int i) { return 4 * i + k; });
-      for (int i = size_ilp * 4; i < n; ++i) p[0] = __fadd_rn(p[0], x[i]);
+        p[k] = cascade_sum(load, size_ilp, [k](int i) { return 4 * i + k; });
+      for (int i = size_ilp * 4; i < n; ++i) p[0] = __fadd_rn(p[0], load(i));
+#pragma unroll
       for (int k = 1; k < 4; ++k) p[0] = __fadd_rn(p[0], p[k]);
       result = __fadd_rn(0.f, p[0]);
     }
@@ -71,21 +76,26 @@ __device__ float torch_cpu_row_sum(const float* x, int n) {
   const int size_ilp = vec_size / 4;
   const int k = lane >> 3;
   const int v = lane & 7;
-  float acc = cascade_sum(x, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
+  float acc = cascade_sum(load, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
   if (k == 0)
-    for (int i = size_ilp * 4; i < vec_size; ++i) acc = __fadd_rn(acc, x[i * 8 + v]);
+    for (int i = size_ilp * 4; i < vec_size; ++i) acc = __fadd_rn(acc, load(i * 8 + v));
   const float a1 = __shfl_sync(0xffffffffu, acc, (v + 8) & 31);
   const float a2 = __shfl_sync(0xffffffffu, acc, (v + 16) & 31);
   const float a3 = __shfl_sync(0xffffffffu, acc, (v + 24) & 31);
   float p = __fadd_rn(__fadd_rn(__fadd_rn(acc, a1), a2), a3);
   float f = 0.f;
   if (lane == 0)
-    for (int i = vec_size * 8; i < n; ++i) f = __fadd_rn(f, x[i]);
+    for (int i = vec_size * 8; i < n; ++i) f = __fadd_rn(f, load(i));
   for (int l = 0; l < 8; ++l) {
     const float pl = __shfl_sync(0xffffffffu, p, l);
     if (lane == 0) f = __fadd_rn(f, pl);
   }
   return __shfl_sync(0xffffffffu, f, 0);
+}
+
+// float32 row sum of x[0..n-1] in the reference's CPU order (one full warp).
+__device__ float torch_cpu_row_sum(const float* x, int n) {
+  return torch_cpu_sum([x](int i) { return x[i]; }, n);
 }
 
 // ---------------------------------------------------------------------------

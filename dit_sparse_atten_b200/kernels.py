@@ -226,6 +226,65 @@ def pack_boolean_rows(route: torch.Tensor):
 
 
 # ----------------------------------------------------------------------------
+# (f4) attention prologue
+# ----------------------------------------------------------------------------
+
+def qkv_prologue(q_proj: torch.Tensor, k_proj: torch.Tensor, v_proj: torch.Tensor, heads: int,
+                 norm_q_weight: torch.Tensor | None = None,
+                 norm_k_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                 rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
+                 perm: torch.Tensor | None = None, norm_q: bool = True, norm_k: bool = True):
+    """RMSNorm(Q), RMSNorm(K), RoPE(Q, K) and the reorder, in one pass.
+
+    ``*_proj``: bf16 ``[B, T, H*D]`` (the ``to_q``/``to_k``/``to_v`` outputs;
+    rows may be strided).  Returns bf16 ``q, k, v`` ``[B, T, H, D]`` with row i
+    taken from token ``perm[i]``.  Bit-identical to the reference's
+    ``rms_norm`` + ``apply_rope`` CPU path (``svg_ops.py:82-92,193-204``)
+    followed by ``index_select(1, perm)``.
+    """
+    device = _require_cuda(q_proj, k_proj, v_proj)
+    if not (q_proj.shape == k_proj.shape == v_proj.shape) or q_proj.dim() != 3:
+        raise ValueError("projections must be [B, T, H*D] with equal shapes")
+    if any(t.dtype != torch.bfloat16 for t in (q_proj, k_proj, v_proj)):
+        raise ValueError("qkv_prologue expects bf16 projections")
+    B, T, C = q_proj.shape
+    if C % heads:
+        raise ValueError(f"{C} features do not split into {heads} heads")
+    D = C // heads
+    if not (q_proj.stride() == k_proj.stride() == v_proj.stride()) or q_proj.stride(-1) != 1:
+        q_proj, k_proj, v_proj = q_proj.contiguous(), k_proj.contiguous(), v_proj.contiguous()
+
+    def weight(w):
+        if w is None:
+            return None
+        if w.numel() != C:
+            raise ValueError("norm weights must have H*D elements")
+        return w.to(device=device, dtype=torch.float32).contiguous()
+    wq, wk = weight(norm_q_weight), weight(norm_k_weight)
+    if (rope_cos is None) != (rope_sin is None):
+        raise ValueError("rope_cos and rope_sin go together")
+    if rope_cos is not None:
+        if tuple(rope_cos.shape) != (T, D // 2) or tuple(rope_sin.shape) != (T, D // 2):
+            raise ValueError(f"rope tables must be [T, D/2] = {(T, D // 2)}")
+        rope_cos = rope_cos.to(device=device, dtype=torch.float32).contiguous()
+        rope_sin = rope_sin.to(device=device, dtype=torch.float32).contiguous()
+    if perm is not None:
+        perm = perm.to(device=device, dtype=torch.int32).contiguous()
+        if perm.numel() != T:
+            raise ValueError("perm must have T entries")
+    outs = [torch.empty((B, T, heads, D), dtype=torch.bfloat16, device=device) for _ in range(3)]
+    if B * T:
+        st = q_proj.stride()
+        _native.call("bsa_qkv_prologue", q_proj.data_ptr(), k_proj.data_ptr(), v_proj.data_ptr(),
+                     B, T, heads, D, st[0], st[1], 1 if norm_q else 0, 1 if norm_k else 0,
+                     _native.ptr(wq), _native.ptr(wk), float(eps), _native.ptr(rope_cos),
+                     _native.ptr(rope_sin), _native.ptr(perm), outs[0].data_ptr(),
+                     outs[1].data_ptr(), outs[2].data_ptr(), _native.err_word(device).data_ptr(),
+                     _stream(device))
+    return tuple(outs)
+
+
+# ----------------------------------------------------------------------------
 # (f3) directional frontier update
 # ----------------------------------------------------------------------------
 

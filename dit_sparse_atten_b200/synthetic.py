@@ -126,6 +126,28 @@ def rope_3d(x, grid, theta=10000.0):
     return out.reshape(x.shape)
 
 
+def prologue_inputs(batch, grid, heads, head_dim=128, seed=0):
+    """Seeded inputs of the attention prologue: bf16 projections
+    ``[B, T, H*D]`` (scaled so that the norm matters), bf16 RMSNorm weights
+    ``[H*D]`` and the complex rotary table ``[T, D/2]`` of Wan's 3-D RoPE
+    (``rope_3d``'s angles)."""
+    g = _generator(seed, "cpu")
+    frames, height, width = grid
+    T, C = frames * height * width, heads * head_dim
+    proj = [(torch.randn((batch, T, C), generator=g) * 2.5).to(torch.bfloat16) for _ in range(3)]
+    weights = [(torch.rand(C, generator=g) + 0.5).to(torch.bfloat16) for _ in range(2)]
+    parts = (head_dim - 4 * (head_dim // 6), 2 * (head_dim // 6), 2 * (head_dim // 6))
+    positions = torch.stack(torch.meshgrid(torch.arange(frames), torch.arange(height),
+                                           torch.arange(width), indexing="ij"), -1).reshape(-1, 3)
+    angles = []
+    for axis, n in enumerate(parts):
+        inv = 10000.0 ** (-torch.arange(0, n, 2, dtype=torch.float64) / n)
+        angles.append(positions[:, axis:axis + 1].double() * inv[None])
+    ang = torch.cat(angles, -1)
+    rotary = torch.polar(torch.ones_like(ang), ang).to(torch.complex64)
+    return proj, weights, rotary
+
+
 def wan_qkv(config, seed=0, device="cpu", dtype=torch.bfloat16):
     """q, k, v ``[B, T, H, D]``: RMS-normalised + 3-D RoPE'd Q/K, N(0,1) V."""
     g = _generator(seed, device)

@@ -97,6 +97,34 @@ BSA_API int bsa_route_select(const float* mass, const uint8_t* prev, int64_t row
                      int32_t* counts, int32_t* indices, uint64_t* kept, void* stream);
 
 /*
+ * (f4) Attention prologue in one pass: for every output row i and batch b,
+ * token t = perm[i] (t = i when perm is NULL) of the projections q_proj /
+ * k_proj / v_proj (bf16 [batch, tokens, heads * head_dim], row strides in
+ * elements) becomes row i of q_out / k_out / v_out (bf16 [batch, tokens,
+ * heads, head_dim] contiguous):
+ *   q, k: RMSNorm over heads * head_dim when norm_q / norm_k is set,
+ *         x * rsqrt(mean(x^2) + eps) * weight in float32 (weight fp32, NULL
+ *         for none), rounded to bf16; then, when rope_cos / rope_sin
+ *         (fp32 [tokens, head_dim / 2]) are given, channel pairs (2j, 2j+1)
+ *         of every head times (cos_j + i sin_j) of token t in float64,
+ *         rounded to bf16;
+ *   v:    copied.
+ * Bit-identical to the reference's CPU path (its mean's summation order
+ * included).  perm entries outside [0, tokens) set BSA_DEVICE_BAD_ROUTE and
+ * their rows are not written.  head_dim % 8 == 0; all pointers 16-byte aligned.
+ * Replaces: attention_backends/wan_diffusers.py:44-56 (norm_q / norm_k through
+ *           svg_ops.rms_norm, svg_ops.py:82-92, and svg_ops.apply_rope,
+ *           svg_ops.py:193-204) and the backend's reorder, spatial.py:86-93.
+ */
+BSA_API int bsa_qkv_prologue(const void* q_proj, const void* k_proj, const void* v_proj,
+                             int64_t batch, int64_t tokens, int64_t heads, int32_t head_dim,
+                             int64_t in_stride_b, int64_t in_stride_t, int32_t norm_q,
+                             int32_t norm_k, const float* norm_q_weight,
+                             const float* norm_k_weight, float eps, const float* rope_cos,
+                             const float* rope_sin, const int32_t* perm, void* q_out,
+                             void* k_out, void* v_out, int32_t* err_word, void* stream);
+
+/*
  * (f3) Frontier of a route: frontier[p, q, k] = route[p, q, k] and some valid
  * neighbour t of q has route[p, t, k] == 0, or some valid neighbour t of k has
  * route[p, q, t] == 0.  route / frontier: uint8 0/1 [planes, blocks, blocks]

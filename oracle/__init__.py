@@ -17,10 +17,12 @@ the hot path:
 * ``oracle.layout``    Morton microtile permutation and the sparse backend's
                        tile-major permutation (``spatial.py:19-183``;
                        ``sparse.py:51-138``)
+* ``oracle.prologue``  the processor's Q/K RMSNorm, RoPE and the reorder
+                       (``wan_diffusers.py:44-56``; ``svg_ops.py:82-92,193-204``)
 
 Pinning: every function is checked against fixtures produced by importing the
 reference itself (``tests/golden/make_golden.py``); see
 ``tests/test_oracle_golden.py``.
 """
 
-from . import attention, layout, route, torch_cpu_order  # noqa: F401
+from . import attention, layout, prologue, route, torch_cpu_order  # noqa: F401

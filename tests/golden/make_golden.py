@@ -27,6 +27,9 @@ Fixtures:
                       digests of Q/K, reference mass of two heads, the
                       reference route and counts.
 * ``blob_routes.npz`` config-2 and config-4 routes from the seeded blob scores.
+* ``prologue.npz``    the Wan processor's Q/K ``rms_norm`` and ``apply_rope``
+                      (``svg_ops.py:82-92,193-204`` CPU path) on seeded
+                      projections, reordered by the reference's layout.
 * ``directional.npz`` ``directional_budget_update`` (``routing.py:97-168``) and
                       the sunk route / frontier of ``_add_first_frame_sink``
                       on the config-3 mass of two heads (plain, and quantised
@@ -55,6 +58,7 @@ sys.path.insert(0, os.environ.get("BSA_REFERENCE", "/root/reference"))
 from attention_backends import flex as ref_flex  # noqa: E402
 from attention_backends import layout_ops as ref_layout_ops  # noqa: E402
 from attention_backends import routing as ref_routing  # noqa: E402
+from attention_backends import svg_ops as ref_svg_ops  # noqa: E402
 from attention_backends import sparse as ref_sparse  # noqa: E402
 from attention_backends import spatial as ref_spatial  # noqa: E402
 
@@ -244,10 +248,35 @@ def directional():
     np.savez_compressed(HERE / "directional.npz", **arrays)
 
 
+PROLOGUE_CASE = {"batch": 1, "grid": (1, 8, 16), "heads": 2, "seed": 12, "eps": 1e-6}
+
+
+def prologue():
+    c = PROLOGUE_CASE
+    (qp, kp, vp), (wq, wk), rotary = synthetic.prologue_inputs(c["batch"], c["grid"], c["heads"],
+                                                               seed=c["seed"])
+    lay = ref_spatial.build_spatial_layout(c["grid"], block_size=128)
+    heads = c["heads"]
+
+    def run(x, w):
+        x = ref_svg_ops.rms_norm(x.contiguous(), w, c["eps"])
+        return x.unflatten(2, (heads, -1)).transpose(1, 2).contiguous()
+    q, k = run(qp, wq), run(kp, wk)
+    q, k = ref_svg_ops.apply_rope(q, k, rotary[None, None])
+    v = vp.unflatten(2, (heads, -1))
+    q, k = q.transpose(1, 2), k.transpose(1, 2)
+    q, k, v = lay.reorder_qkv(q.contiguous(), k.contiguous(), v.contiguous())
+    np.savez_compressed(
+        HERE / "prologue.npz", proj_sha=np.array([sha256(x) for x in (qp, kp, vp)]),
+        weight_sha=np.array([sha256(w) for w in (wq, wk)]), rotary_sha=sha256(torch.view_as_real(rotary)),
+        perm=lay.permutation_cpu.numpy(), q=q.contiguous().view(torch.int16).numpy(),
+        k=k.contiguous().view(torch.int16).numpy(), v=v.contiguous().view(torch.int16).numpy())
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     only = set(sys.argv[1:])
-    for fn in (kat, layouts, config1, route_480p, blob_routes, config3, directional):
+    for fn in (kat, layouts, config1, route_480p, blob_routes, config3, directional, prologue):
         if only and fn.__name__ not in only:
             continue
         t = time.time()
