@@ -460,25 +460,49 @@ class FlexReuseBackend:
     def _dense_call(self, q, k, v, **kw):
         return self.dense(q, k, v, **kw)
 
+    def packed_layout_for(self, tokens):
+        """The spatial layout this backend's next call (under the current
+        routing context) would pack its inputs with, or None.  A caller that
+        already produced q, k, v in that order (the fused prologue) passes it
+        back as ``packed_layout=`` and the backend skips its own reorder; the
+        output is still returned in the original token order."""
+        attention_id, _step, _branch, grid = self._context()
+        if self.config.first_layer_dense and attention_id == 0:
+            return None
+        return self._spatial_layout(grid, tokens)
+
     def __call__(self, q, k, v, q_lens=None, k_lens=None, dropout_p=0.0, softmax_scale=None,
                  q_scale=None, causal=False, window_size=(-1, -1), deterministic=False,
                  dtype=torch.bfloat16, version=None, **kwargs):
+        # Inputs already in route-block order of this layout (the fused
+        # prologue's output, see packed_layout_for); not part of the
+        # reference's signature, which swallows unknown keywords.
+        packed = kwargs.pop("packed_layout", None)
         dense_kw = dict(q_lens=q_lens, k_lens=k_lens, dropout_p=dropout_p,
                         softmax_scale=softmax_scale, q_scale=q_scale, causal=causal,
                         window_size=window_size, deterministic=deterministic, dtype=dtype,
                         version=version, **kwargs)
+
+        def dense_unpacked():
+            # dense attention is order-equivariant: restore a packed result
+            out = self._dense_call(q, k, v, **dense_kw)
+            return packed.restore(out.contiguous()) if packed is not None else out
+
         supported = (q.shape[0] == 1 and q.shape[1] == k.shape[1] and dropout_p == 0
                      and not causal and window_size == (-1, -1))
         if not supported:
-            return self._dense_call(q, k, v, **dense_kw)
+            return dense_unpacked()
 
         attention_id, step, branch, grid = self._context()
         if self.config.first_layer_dense and attention_id == 0:
             self.phase_counts["first_layer_dense"] += 1
-            return self._dense_call(q, k, v, **dense_kw)
+            return dense_unpacked()
         layout = self._spatial_layout(grid, q.shape[1])
         if self.config.spatial_reorder and layout is None:
-            return self._dense_call(q, k, v, **dense_kw)
+            return dense_unpacked()
+        if packed is not None and (layout is None or packed.signature != layout.signature):
+            q, k, v = (packed.restore(x.contiguous()) for x in (q, k, v))
+            packed = None
 
         output_dtype = q.dtype
         q = q.to(dtype)
@@ -486,7 +510,7 @@ class FlexReuseBackend:
         v = v.to(dtype)
         if q_scale is not None:
             q = q * q_scale
-        if layout is not None:
+        if layout is not None and packed is None:
             q, k, v = layout.reorder_qkv(q, k, v)
 
         def finish(output):
