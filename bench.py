@@ -437,6 +437,7 @@ def main(argv=None):
             stages.update(route_stage(cfg, qp, kp, local_route, kernels, device, stream,
                                       layout.neighbors(device)))
             stages.update(bootstrap_stage(cfg, qp, kp, vp, kernels, stream))
+            stages.update(prologue_stage(cfg, layout, kernels, device, stream))
 
     peaks, peak_src = load_peaks()
     local_flops = kept_flops(local_route, cfg.tokens, cfg.block, cfg.head_dim)
@@ -546,6 +547,28 @@ def bootstrap_stage(cfg, qp, kp, vp, kernels, stream):
     B, T, H, D = qp.shape
     return {"bootstrap_dense_and_mass_ms": ms,
             "bootstrap_dense_tflops": 4.0 * B * H * T * T * D / ms / 1e9}
+
+
+def prologue_stage(cfg, layout, kernels, device, stream):
+    """The processor's prologue for this layer (both branches): Q/K RMSNorm,
+    RoPE and the reorder into route-block order in one pass (HBM-bound)."""
+    from dit_sparse_atten_b200 import _native, synthetic
+    proj, weights, rotary = synthetic.prologue_inputs(cfg.batch, cfg.grid, cfg.heads, seed=9)
+    proj = [p.to(device) for p in proj]
+    wq, wk = (w.float().to(device) for w in weights)
+    cos, sin = rotary.real.float().to(device), rotary.imag.float().to(device)
+    perm = layout.permutation_cpu.to(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    kernels.qkv_prologue(*proj, cfg.heads, wq, wk, 1e-6, cos, sin, perm=perm)
+    ev[0].record(stream)
+    kernels.qkv_prologue(*proj, cfg.heads, wq, wk, 1e-6, cos, sin, perm=perm)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    ms = ev[0].elapsed_time(ev[1])
+    # read and write Q, K, V once, plus the rotary tables
+    algorithmic = 6 * proj[0].numel() * 2 + 2 * cos.numel() * 4
+    return {"prologue_ms": ms, "prologue_hbm_gbs": algorithmic / ms / 1e6}
 
 
 def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total_flops):
