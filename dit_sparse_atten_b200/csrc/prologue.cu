@@ -86,7 +86,7 @@ __device__ void norm_rope_row(const __nv_bfloat16* __restrict__ src, __nv_bfloat
   }
 }
 
-__global__ void __launch_bounds__(kPrologueThreads) qkv_prologue_kernel(PrologueArgs a) {
+__global__ void __launch_bounds__(kPrologueThreads, 4) qkv_prologue_kernel(PrologueArgs a) {
   const int C = a.heads * a.head_dim;
   const int64_t rows = a.batch * a.tokens;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kPrologueThreads / 32);

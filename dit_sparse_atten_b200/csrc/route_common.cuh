@@ -33,7 +33,15 @@ __device__ float cascade_sum(Load load, int size, IndexFn index) {
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
   int i = 0;
   while (i + level_step <= size) {
-    for (int j = 0; j < level_step; ++j, ++i) acc0 = __fadd_rn(acc0, load(index(i)));
+    // level_step is a power of two >= 16: items go in groups of 8, all loaded
+    // before any is added (the additions keep their order).
+    for (int j = 0; j < level_step; j += 8, i += 8) {
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = load(index(i + u));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc0 = __fadd_rn(acc0, x[u]);
+    }
     acc1 = __fadd_rn(acc1, acc0);
     acc0 = 0.f;
     if ((i & (level_mask << level_power)) != 0) continue;
