@@ -17,7 +17,8 @@
 //      the best neighbour along Q and along K, eligibility, and the scatter of
 //      the Q, K and joint candidates (byte stores of 1; concurrent stores to a
 //      cell write the same value).
-//   2. directional_select_kernel, one CTA per row: candidates & ~prev, pool,
+//   2. directional_select_warp_kernel (one warp per row, n <= 512) or
+//      directional_select_kernel (one CTA per row): candidates & ~prev, pool,
 //      exploration, prior score, fixed budget, sink, CSR, kept counter.
 //   3. frontier_kernel over the new route (only when a frontier is wanted).
 // Float arithmetic whose last bit decides a route follows the reference's
@@ -230,6 +231,102 @@ __global__ void __launch_bounds__(kSelThreads) directional_select_kernel(Directi
                 a.kept != nullptr ? a.kept + row / a.rows_per_group : nullptr);
 }
 
+// Warp-per-row version of directional_select_kernel for n <= 512 (same
+// outputs): the two selections use the register sort of route_common.cuh.
+constexpr int kDirWarps = 4;  // rows per CTA
+
+struct DirWarpSmem {
+  SortPair pairs[kWarpSelMaxCols];                      // tie replay scratch
+  float vals[kWarpSelMaxCols + kWarpSelMaxCols / 16];   // mass at vidx(i)
+  float score[kWarpSelMaxCols + kWarpSelMaxCols / 16];  // selection score at vidx(i)
+  uint8_t fprev[kWarpSelMaxCols], fcand[kWarpSelMaxCols], fpool[kWarpSelMaxCols],
+      fexpl[kWarpSelMaxCols], froute[kWarpSelMaxCols];
+};
+
+template <int ITEMS>
+__global__ void __launch_bounds__(kDirWarps * 32) directional_select_warp_kernel(
+    DirectionalArgs a) {
+  __shared__ DirWarpSmem smem_all[kDirWarps];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = a.n;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kDirWarps + warp;
+  if (row >= a.planes * n) return;  // warp-uniform; no CTA barrier below
+  DirWarpSmem& sm = smem_all[warp];
+  const size_t base = static_cast<size_t>(row) * n;
+  float* vals = sm.vals;
+  float* score = sm.score;
+
+  // ---- pool = prev | (candidates & ~prev) ---------------------------------
+  int prev_local = 0;
+  for (int i = lane; i < n; i += 32) {
+    vals[vidx(i)] = a.mass[base + i];
+    const uint8_t p = a.prev[base + i] ? 1 : 0;
+    const uint8_t c = (a.candidates[base + i] && !p) ? 1 : 0;
+    sm.fprev[i] = p;
+    sm.fcand[i] = c;
+    sm.fpool[i] = p | c;
+    sm.fexpl[i] = 0;
+    prev_local += p;
+  }
+  const int prev_count = __reduce_add_sync(kFull, prev_local);
+  __syncwarp();
+
+  // ---- exploration: the explore_count highest masses outside the pool -----
+  if (a.explore_count > 0) {
+    for (int i = lane; i < n; i += 32) score[vidx(i)] = sm.fpool[i] ? -INFINITY : vals[vidx(i)];
+    __syncwarp();
+    warp_mark_first_desc<ITEMS>(score, n, a.explore_count, sm.pairs, sm.fexpl);
+    for (int i = lane; i < n; i += 32) sm.fpool[i] |= sm.fexpl[i];
+    __syncwarp();
+  }
+  int pool_local = 0;
+  for (int i = lane; i < n; i += 32) pool_local += sm.fpool[i];
+  const int pool_count = __reduce_add_sync(kFull, pool_local);
+
+  // ---- score = mass + p*mean(mass)*prev [+ bonus*mean(mass)*candidates] ----
+  const float sum = torch_cpu_sum([vals](int i) { return vals[vidx(i)]; }, n);
+  const float row_scale = __fdiv_rn(sum, static_cast<float>(n));
+  const float bump = __fmul_rn(row_scale, a.persistence);
+  const float cbump = __fmul_rn(row_scale, a.candidate_bonus);
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) {
+    float s = __fadd_rn(vals[vidx(i)], __fmul_rn(bump, sm.fprev[i] ? 1.f : 0.f));
+    if (a.candidate_bonus != 0.f) s = __fadd_rn(s, __fmul_rn(cbump, sm.fcand[i] ? 1.f : 0.f));
+    score[vidx(i)] = sm.fpool[i] ? s : -INFINITY;
+  }
+  __syncwarp();
+
+  // ---- fixed budget: ceil(#prev * scale) in [1, cap], at most the pool -----
+  int count = static_cast<int>(ceilf(__fmul_rn(static_cast<float>(prev_count), a.budget_scale)));
+  count = min(max(count, 1), a.cap);
+  count = max(min(count, pool_count), 1);
+  warp_mark_first_desc<ITEMS>(score, n, count, sm.pairs, sm.froute);
+
+  // ---- outputs before the sink, then the sink and the CSR ----------------
+  for (int i = lane; i < n; i += 32) {
+    const uint8_t r = sm.froute[i] & sm.fpool[i];
+    const uint8_t p = sm.fprev[i];
+    a.candidates[base + i] = sm.fcand[i];
+    if (a.exploration != nullptr) a.exploration[base + i] = sm.fexpl[i];
+    if (a.dropped != nullptr) a.dropped[base + i] = p & (r ^ 1);
+    if (a.added != nullptr) a.added[base + i] = r & (p ^ 1);
+    sm.froute[i] = (r || i < a.sink_blocks) ? 1 : 0;
+  }
+  __syncwarp();
+  warp_write_csr_row(sm.froute, n, base, a.indices, a.route_out,
+                     a.counts != nullptr ? a.counts + row : nullptr,
+                     a.kept != nullptr ? a.kept + row / a.rows_per_group : nullptr);
+}
+
+template <int ITEMS>
+cudaError_t launch_directional_warp(const DirectionalArgs& a, int64_t rows, cudaStream_t stream) {
+  const int64_t ctas = (rows + kDirWarps - 1) / kDirWarps;
+  directional_select_warp_kernel<ITEMS>
+      <<<static_cast<unsigned>(ctas), kDirWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 unsigned cell_grid(int64_t cells, int num_sms) {
   const int64_t want = (cells + kCellThreads - 1) / kCellThreads;
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
@@ -256,6 +353,11 @@ cudaError_t launch_directional_update(const DirectionalArgs& a, cudaStream_t str
   candidate_scatter_kernel<<<cell_grid(rows * a.n, num_sms), kCellThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (a.n <= 32) return launch_directional_warp<1>(a, rows, stream);
+  if (a.n <= 64) return launch_directional_warp<2>(a, rows, stream);
+  if (a.n <= 128) return launch_directional_warp<4>(a, rows, stream);
+  if (a.n <= 256) return launch_directional_warp<8>(a, rows, stream);
+  if (a.n <= kWarpSelMaxCols) return launch_directional_warp<16>(a, rows, stream);
   int np = 1;
   while (np < a.n) np <<= 1;
   const size_t smem = static_cast<size_t>(np) * 8 + static_cast<size_t>(a.n) * 13 + 16;

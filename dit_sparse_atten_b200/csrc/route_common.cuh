@@ -2,8 +2,10 @@
 // selection in route_select.cu, the directional budget update in
 // directional.cu): the reference's PyTorch CPU float32 row sum, a block-wide
 // sort of (value descending, block id ascending), the reference's unstable
-// argsort tie order, and the CSR partition of a selected row.  Every function
-// is called by all kSelThreads threads of the CTA unless it says otherwise.
+// argsort tie order, and the CSR partition of a selected row; then the same
+// steps for one warp per row (register bitonic sort of value keys).  Every
+// block-wide function is called by all kSelThreads threads of the CTA, every
+// warp_* function by all 32 lanes of a warp.
 #pragma once
 
 #include "bsa_kernels.h"
@@ -344,6 +346,157 @@ __device__ void write_csr_row(const uint8_t* flags, int n, size_t base, int32_t*
     sel_before += f;
   }
   if (tid == 0) {
+    if (count_out != nullptr) *count_out = total;
+    if (kept_slot != nullptr) atomicAdd(kept_slot, static_cast<unsigned long long>(total));
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Warp-per-row helpers (rows of up to kWarpSelMaxCols blocks).  A row's values
+// sit in shared memory at vidx(e) (one pad word per 16, so lane-major register
+// loads are conflict-free); sort keys live in registers, ITEMS per lane, lane l
+// holding positions [l*ITEMS, (l+1)*ITEMS).  Called by all 32 lanes.
+// ---------------------------------------------------------------------------
+constexpr int kWarpSelMaxCols = 512;
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ int vidx(int e) { return e + (e >> 4); }
+
+// Ascending in this key = descending in value (-0 and +0 share a key).
+__device__ __forceinline__ uint32_t desc_value_key(float v) { return ~float_order_key(v); }
+
+__device__ __forceinline__ float desc_key_value(uint32_t key) {
+  const uint32_t k = ~key;
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+template <int ITEMS>
+__device__ __forceinline__ void warp_sort_ascending(uint32_t (&k)[ITEMS]) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kLog = (ITEMS == 1 ? 5 : ITEMS == 2 ? 6 : ITEMS == 4 ? 7 : ITEMS == 8 ? 8 : 9);
+#pragma unroll
+  for (int ls = 1; ls <= kLog; ++ls) {
+    const int size = 1 << ls;
+    uint32_t flip[ITEMS];
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      flip[j] = ((lane * ITEMS + j) & size) ? 0xffffffffu : 0u;   // 0 in the last phase
+      k[j] ^= flip[j];
+    }
+#pragma unroll
+    for (int ss = ls - 1; ss >= 0; --ss) {
+      const int stride = 1 << ss;
+      if (stride < ITEMS) {
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+          if (j & stride) continue;
+          const uint32_t x = k[j], y = k[j | stride];
+          k[j] = min(x, y);
+          k[j | stride] = max(x, y);
+        }
+      } else {
+        const int lstride = stride / ITEMS;
+        const bool lower = (lane & lstride) == 0;
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+          const uint32_t o = __shfl_xor_sync(kFull, k[j], lstride);
+          k[j] = lower ? min(k[j], o) : max(k[j], o);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) k[j] ^= flip[j];
+  }
+}
+
+// Element pos (0 <= pos < 32*ITEMS) of a per-lane register array.
+template <int ITEMS, typename T>
+__device__ __forceinline__ T lane_item(const T (&x)[ITEMS], int pos) {
+  const int lane = threadIdx.x & 31;
+  T v = T(0);
+#pragma unroll
+  for (int j = 0; j < ITEMS; ++j)
+    if (lane * ITEMS + j == pos) v = x[j];
+  return __shfl_sync(kFull, v, pos / ITEMS);
+}
+
+
+// Bitonic network of 32*ITEMS keys for one warp.
+template <int ITEMS>
+__device__ __forceinline__ void warp_load_sorted_keys(const float* vals, int n,
+                                                      uint32_t (&key)[ITEMS]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < ITEMS; ++j) {
+    const int e = lane * ITEMS + j;
+    key[j] = e < n ? desc_value_key(vals[vidx(e)]) : 0xffffffffu;
+  }
+  warp_sort_ascending<ITEMS>(key);
+}
+
+// flags[i] = 1 for the first `count` entries of the reference's
+// `vals.argsort(descending=True)` (vals at vidx(i)), 0 for the rest, given the
+// sort key `cut` of the value at position count - 1 and whether equal values
+// straddle the cut (then lane 0 replays the reference's introsort in `pairs`).
+__device__ void warp_flags_from_cut(const float* vals, int n, int count, uint32_t cut, bool tie,
+                                    SortPair* pairs, uint8_t* flags) {
+  const int lane = threadIdx.x & 31;
+  if (!tie) {
+    for (int i = lane; i < n; i += 32) flags[i] = desc_value_key(vals[vidx(i)]) <= cut ? 1 : 0;
+  } else {
+    __syncwarp();
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) pairs[i] = SortPair{vals[vidx(i)], i};
+      introsort_desc(pairs, n);
+    }
+    __syncwarp();
+    for (int r = lane; r < n; r += 32) flags[pairs[r].i] = r < count ? 1 : 0;
+  }
+  __syncwarp();
+}
+
+// Warp version of mark_first_desc: sorts the row itself.
+template <int ITEMS>
+__device__ void warp_mark_first_desc(const float* vals, int n, int count, SortPair* pairs,
+                                     uint8_t* flags) {
+  const int lane = threadIdx.x & 31;
+  if (count >= n || count <= 0) {
+    for (int i = lane; i < n; i += 32) flags[i] = count > 0 ? 1 : 0;
+    __syncwarp();
+    return;
+  }
+  uint32_t key[ITEMS];
+  warp_load_sorted_keys<ITEMS>(vals, n, key);
+  const uint32_t cut = lane_item<ITEMS>(key, count - 1);
+  const bool tie = lane_item<ITEMS>(key, count) == cut;
+  warp_flags_from_cut(vals, n, count, cut, tie, pairs, flags);
+}
+
+// Warp version of write_csr_row (same outputs).
+__device__ void warp_write_csr_row(const uint8_t* flags, int n, size_t base, int32_t* indices,
+                                   uint8_t* route_out, int32_t* count_out,
+                                   unsigned long long* kept_slot) {
+  const int lane = threadIdx.x & 31;
+  int total = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    total += __popc(__ballot_sync(kFull, i < n && flags[i] != 0));
+  }
+  const unsigned below_mask = (1u << lane) - 1u;
+  int sel = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const bool f = i < n && flags[i] != 0;
+    const unsigned m = __ballot_sync(kFull, f);
+    const int before = sel + __popc(m & below_mask);
+    if (i < n) {
+      if (indices != nullptr) indices[base + (f ? before : total + (i - before))] = i;
+      if (route_out != nullptr) route_out[base + i] = static_cast<uint8_t>(f);
+    }
+    sel += __popc(m);
+  }
+  if (lane == 0) {
     if (count_out != nullptr) *count_out = total;
     if (kept_slot != nullptr) atomicAdd(kept_slot, static_cast<unsigned long long>(total));
   }

@@ -164,6 +164,40 @@ def test_select_tie_heavy_rows_match_oracle(cols):
         check_csr(r, ref)
 
 
+def _row_families(rng, rows, cols):
+    """Rows that take each branch of the selection kernels: wide-range masses
+    (the parallel float64 prefix sums are exact), masses spanning ~70 decades
+    (not provably exact: serial scan), zeros, negative values (non-monotone
+    prefix sums), and exactly tied values."""
+    u = rng.random((rows, cols))
+    wide = u ** 4
+    decades = np.exp(-rng.random((rows, cols)) * 160.0)
+    zeros = np.where(rng.random((rows, cols)) < 0.4, 0.0, u)
+    signed = rng.standard_normal((rows, cols))
+    tied = rng.integers(0, 3, (rows, cols)) / 2.0
+    return [x.astype(np.float32) for x in (wide, decades, zeros, signed, tied)]
+
+
+@pytest.mark.parametrize("cols", [1, 2, 7, 31, 32, 33, 64, 65, 128, 129, 255, 256, 300, 450,
+                                  511, 512, 513])
+def test_select_row_families_every_width(cols):
+    """Every register width of the warp kernel (and the CTA kernel above 512
+    blocks) against the oracle, with and without the prior, caps from 1 to
+    all blocks."""
+    rng = np.random.default_rng(1000 + cols)
+    for mass in _row_families(rng, 24, cols):
+        prev = rng.random(mass.shape) < 0.5
+        for target, keep in ((0.95, 0.625), (1.0, 1.0), (0.5, 1e-9), (0.999, 0.9)):
+            r = select(mass, target=target, keep=keep)
+            check_csr(r, oroute.top_mass_route(mass, target, keep))
+            r = select(mass, prev, 0.5, target, keep, sink=min(cols, 3))
+            ref = oroute.sampled_route(mass, prev, 0.5, target, keep)
+            ref[..., :3] = True
+            check_csr(r, ref)
+            kept = r.kept.cpu().numpy()
+            assert kept.tolist() == ref.reshape(len(kept), -1).sum(-1).tolist()
+
+
 def test_select_random_keep_and_target_sweep():
     rng = np.random.default_rng(3)
     mass = (rng.random((8, 40, 450)) ** 4).astype(np.float32)
