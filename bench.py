@@ -525,7 +525,8 @@ def route_stage(cfg, qp, kp, route, kernels, device, stream, neighbors):
     sampled = 2 * B * H * Qb * 16 * cfg.head_dim * 2
     select_bytes = B * H * Qb * Qb * (4 + 1 + 1 + 4) + B * H * Qb * 4
     return {"route_mass_ms": mass_ms, "route_select_ms": select_ms,
-            "route_mass_tflops": 2 * 2 * B * H * (Qb * 16) ** 2 * cfg.head_dim / mass_ms / 1e9,
+            # algorithmic: one Q_s K_s^T product (the kernel streams the keys once)
+            "route_mass_tflops": 2 * B * H * (Qb * 16) ** 2 * cfg.head_dim / mass_ms / 1e9,
             "route_select_hbm_gbs": select_bytes / select_ms / 1e6,
             "directional_update_ms": directional_ms,
             "directional_update_hbm_gbs": directional_bytes / directional_ms / 1e6,

@@ -34,6 +34,9 @@ SIGNATURES = {
     "bsa_sampled_mass": ([_P, _P, _I64, _I64, _I32, _I32, _I32, _P, _F32, _I32, _P, _P, _P], _I32),
     "bsa_sampled_mass_noalloc": ([_P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F32, _I32, _P, _P,
                                   _P], _I32),
+    "bsa_sampled_mass_workspace_bytes": ([_I64, _I64, _I32, _I32], _I64),
+    "bsa_sampled_mass_onepass": ([_P, _P, _I64, _I64, _I32, _I32, _I32, _P, _F32, _I32, _P, _I64,
+                                  _P, _P, _P], _I32),
     "bsa_exact_block_mass": ([_P, _P, _I64, _I64, _I64, _I32, _I32, _F32, _P, _P, _P, _P], _I32),
     "bsa_attention_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _P, _P, _I32,
                            _I32, _I32, _F32, _P, _I64, _I64, _I64, _P, _P, _P], _I32),

@@ -102,6 +102,50 @@ int encode_bhtd(CUtensorMap* map, const void* ptr, int64_t B, int64_t T, int64_t
 
 }  // namespace
 
+namespace {
+
+// Checks and tensor maps shared by the two sampled-mass entry points.
+int sampled_mass_setup(const void* sampled_q, const void* sampled_k, int64_t batch,
+                       int64_t heads, int32_t q_blocks, int32_t samples, int32_t head_dim,
+                       const float* block_bias, float scale, int32_t round_bf16, float* mass,
+                       int32_t* err_word, CUtensorMap* tq, CUtensorMap* tk, bsa::MassArgs* a) {
+  if (sampled_q == nullptr || sampled_k == nullptr || block_bias == nullptr || mass == nullptr ||
+      err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (samples != 1 && samples != 2 && samples != 4 && samples != 8 && samples != 16 &&
+      samples != 32)
+    return fail(BSA_ERR_UNSUPPORTED, "samples must be a power of two <= 32 (got %d)", samples);
+  if (q_blocks <= 0 || q_blocks > 4096)
+    return fail(BSA_ERR_UNSUPPORTED, "q_blocks must be in [1, 4096] (got %d)", q_blocks);
+  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/heads");
+  const int64_t n_rows = static_cast<int64_t>(q_blocks) * samples;
+  bool tm = false;
+  int rc = encode_bhtd(tq, sampled_q, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
+                       heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  rc = encode_bhtd(tk, sampled_k, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
+                   heads * head_dim, head_dim, 128, &tm);
+  if (rc != BSA_OK) return rc;
+  if (tm) return fail(BSA_ERR_INVALID_ARGUMENT, "sampled tensors must be [B, N, H, D] contiguous");
+  *a = bsa::MassArgs{};
+  a->batch = batch;
+  a->heads = heads;
+  a->n_rows = n_rows;
+  a->samples = samples;
+  a->q_blocks = q_blocks;
+  a->scale = scale;
+  a->round_bf16 = round_bf16;
+  a->block_bias = block_bias;
+  a->mass_scale = 1.0f / static_cast<float>(samples);
+  a->mass = mass;
+  a->err_word = err_word;
+  return BSA_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int bsa_version(void) { return 10000; }
@@ -315,41 +359,49 @@ int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch
                      int32_t q_blocks, int32_t samples, int32_t head_dim,
                      const float* block_bias, float scale, int32_t round_bf16, float* mass,
                      int32_t* err_word, void* stream) {
-  if (sampled_q == nullptr || sampled_k == nullptr || block_bias == nullptr || mass == nullptr ||
-      err_word == nullptr)
-    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
-  if (head_dim != 128) return fail(BSA_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
-  if (samples != 1 && samples != 2 && samples != 4 && samples != 8 && samples != 16 &&
-      samples != 32)
-    return fail(BSA_ERR_UNSUPPORTED, "samples must be a power of two <= 32 (got %d)", samples);
-  if (q_blocks <= 0 || q_blocks > 4096)
-    return fail(BSA_ERR_UNSUPPORTED, "q_blocks must be in [1, 4096] (got %d)", q_blocks);
-  if (batch <= 0 || heads <= 0 || batch > 65535 || heads > 65535)
-    return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/heads");
-  const int64_t n_rows = static_cast<int64_t>(q_blocks) * samples;
   CUtensorMap tq, tk;
-  bool tm = false;
-  int rc = encode_bhtd(&tq, sampled_q, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
-                       heads * head_dim, head_dim, 128, &tm);
+  bsa::MassArgs a;
+  const int rc = sampled_mass_setup(sampled_q, sampled_k, batch, heads, q_blocks, samples,
+                                    head_dim, block_bias, scale, round_bf16, mass, err_word, &tq,
+                                    &tk, &a);
   if (rc != BSA_OK) return rc;
-  rc = encode_bhtd(&tk, sampled_k, batch, n_rows, heads, head_dim, n_rows * heads * head_dim,
-                   heads * head_dim, head_dim, 128, &tm);
-  if (rc != BSA_OK) return rc;
-  if (tm) return fail(BSA_ERR_INVALID_ARGUMENT, "sampled tensors must be [B, N, H, D] contiguous");
-  bsa::MassArgs a{};
-  a.batch = batch;
-  a.heads = heads;
-  a.n_rows = n_rows;
-  a.samples = samples;
-  a.q_blocks = q_blocks;
-  a.scale = scale;
-  a.round_bf16 = round_bf16;
-  a.block_bias = block_bias;
-  a.mass_scale = 1.0f / static_cast<float>(samples);
-  a.mass = mass;
-  a.err_word = err_word;
   cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass launch");
+  return ok();
+}
+
+int64_t bsa_sampled_mass_workspace_bytes(int64_t batch, int64_t heads, int32_t q_blocks,
+                                         int32_t samples) {
+  if (batch <= 0 || heads <= 0 || q_blocks <= 0 || samples <= 0) return 0;
+  const int64_t n_rows = static_cast<int64_t>(q_blocks) * samples;
+  return batch * heads * n_rows * (static_cast<int64_t>(q_blocks) + 1) * 4;
+}
+
+int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_k, int64_t batch,
+                             int64_t heads, int32_t q_blocks, int32_t samples, int32_t head_dim,
+                             const float* block_bias, float scale, int32_t round_bf16,
+                             float* workspace, int64_t workspace_bytes, float* mass,
+                             int32_t* err_word, void* stream) {
+  const int64_t need = bsa_sampled_mass_workspace_bytes(batch, heads, q_blocks, samples);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "workspace of %lld bytes needed (got %lld)",
+                static_cast<long long>(need), static_cast<long long>(workspace_bytes));
+  if (reinterpret_cast<uintptr_t>(workspace) & 15)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  if (batch * heads > 65535) return fail(BSA_ERR_UNSUPPORTED, "batch * heads must be <= 65535");
+  CUtensorMap tq, tk;
+  bsa::MassArgs a;
+  const int rc = sampled_mass_setup(sampled_q, sampled_k, batch, heads, q_blocks, samples,
+                                    head_dim, block_bias, scale, round_bf16, mass, err_word, &tq,
+                                    &tk, &a);
+  if (rc != BSA_OK) return rc;
+  a.block_lse = workspace;
+  a.row_lse = workspace + batch * heads * a.n_rows * q_blocks;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, s);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_onepass launch");
+  e = bsa::launch_sampled_mass_reduce(a, s);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_onepass reduce launch");
   return ok();
 }
 

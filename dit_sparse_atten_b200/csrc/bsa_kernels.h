@@ -101,9 +101,18 @@ struct MassArgs {
   const float* lse;               // [B, H, n_rows] natural-log LSE per query row, or null
   float* mass;                    // [B, H, Qb, Qb]
   int* err_word;
+  // One-pass mode (S <= 32, lse null): instead of `mass`, the kernel writes
+  // block_lse[B, H, Qb, n_rows] = log2 of each row's exponential sum over each
+  // key block's S keys (absolute: stabiliser included) and row_lse[B, H, n_rows]
+  // = log2 of the row's total; launch_sampled_mass_reduce then forms the mass.
+  float* block_lse;
+  float* row_lse;
 };
 cudaError_t launch_sampled_mass(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                                 const MassArgs& args, cudaStream_t stream);
+// mass[b, h, qb, kb] = mass_scale * sum_{s < S} 2^(block_lse[b, h, kb, qb S + s]
+//                                                 - row_lse[b, h, qb S + s])
+cudaError_t launch_sampled_mass_reduce(const MassArgs& args, cudaStream_t stream);
 
 // ---- (b) sampled block mass without a caller workspace ---------------------
 // Size of the module-level scratch (a static __device__ array) that

@@ -158,9 +158,11 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int n_tiles = static_cast<int>((a.n_rows + kTile - 1) / kTile);
-  // With the log-sum-exp given, pass 1 is skipped.
+  // With the log-sum-exp given, pass 1 is skipped; in one-pass mode pass 1
+  // emits per-block log sums and pass 2 is left to the reduction kernel.
+  const bool emit = !kWide && a.block_lse != nullptr;
   const int pass1 = a.lse != nullptr ? 0 : n_tiles;
-  const int steps = pass1 + n_tiles;
+  const int steps = emit ? n_tiles : pass1 + n_tiles;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
@@ -281,8 +283,39 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
                                fmaxf(m8[6], m8[7]));
         const float m_new = fmaxf(m2, mx);
         // A half-row whose keys so far are all past the sequence (few sampled
-        // rows) keeps (-inf, 0): -inf - -inf would be NaN.
-        if (m_new != -INFINITY) {
+        // rows) keeps (-inf, 0): -inf - -inf would be NaN.  Its blocks are
+        // all past the sequence too, so one-pass mode has nothing to write.
+        if (emit && m_new != -INFINITY) {
+          // One pass: exponentials summed per key block, relative to m_new;
+          // each block's log2 sum (absolute) goes to the workspace.
+          const float2 nm = make_float2(-m_new, -m_new);
+          float g[kHalfBlocks];
+#pragma unroll
+          for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
+#pragma unroll
+          for (int p = 0; p < 32; ++p) {
+            const float2 t = __fadd2_rn(y[p], nm);
+            const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
+            if constexpr (LOG2S == 0) {
+              g[2 * p] += e.x;
+              g[2 * p + 1] += e.y;
+            } else {
+              g[(2 * p) >> LOG2S] += e.x + e.y;
+            }
+          }
+          float tot = 0.f;
+#pragma unroll
+          for (int gi = 0; gi < kHalfBlocks; ++gi) tot += g[gi];
+          l = l * ex2_approx(m2 - m_new) + tot;
+          m2 = m_new;
+          if (qrow < a.n_rows) {
+            const int64_t kb0 = key0 >> LOG2S;
+            float* dst = a.block_lse + (out_rows + kb0) * a.n_rows + qrow;
+#pragma unroll
+            for (int gi = 0; gi < kHalfBlocks; ++gi)
+              if (kb0 + gi < a.q_blocks) dst[gi * a.n_rows] = m_new + __log2f(g[gi]);
+          }
+        } else if (m_new != -INFINITY) {
           const float2 nm = make_float2(-m_new, -m_new);
           float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                            make_float2(0.f, 0.f)};
@@ -307,6 +340,8 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
           const float l_all = l * ex2_approx(m2 - m_all) + o.y * ex2_approx(o.x - m_all);
           // 2^(y - m_fold) = 2^(y - m_all) / l_all
           m_fold = m_all + __log2f(l_all);
+          if (emit && half == 0 && qrow < a.n_rows)
+            a.row_lse[(static_cast<int64_t>(b) * a.heads + h) * a.n_rows + qrow] = m_fold;
         }
       } else {
         // Pass 2: normalised probabilities summed per key block, then over the
@@ -410,6 +445,61 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   }
 }
 
+// One-pass mode, second step: one CTA per 32 x 32 (query block, key block)
+// tile of one (b, h); warp w sums key blocks kb0 + 4w .. 4w + 3 for the 32
+// query blocks (one per lane, its S rows contiguous in block_lse), rows in
+// order; the tile is written row-major through shared memory.
+template <int LOG2S>
+__global__ void __launch_bounds__(256) sampled_mass_reduce_kernel(const MassArgs a) {
+  constexpr int S = 1 << LOG2S;
+  __shared__ float tile[32][33];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qb0 = blockIdx.x * 32;
+  const int kb0 = blockIdx.y * 32;
+  const int64_t bh = blockIdx.z;
+  const int Qb = a.q_blocks;
+  const int qb = qb0 + lane;
+  float lse[S];
+  if (qb < Qb) {
+    const float* lr = a.row_lse + bh * a.n_rows + static_cast<int64_t>(qb) * S;
+#pragma unroll
+    for (int s = 0; s < S; ++s) lse[s] = lr[s];
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int kl = warp * 4 + c;
+    const int kb = kb0 + kl;
+    float sum = 0.f;
+    if (qb < Qb && kb < Qb) {
+      const float* v = a.block_lse + (bh * Qb + kb) * a.n_rows + static_cast<int64_t>(qb) * S;
+      float x[S];
+      if constexpr (S >= 4) {
+#pragma unroll
+        for (int s = 0; s < S; s += 4) {
+          const float4 t = __ldcs(reinterpret_cast<const float4*>(v + s));
+          x[s] = t.x;
+          x[s + 1] = t.y;
+          x[s + 2] = t.z;
+          x[s + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int s = 0; s < S; ++s) x[s] = __ldcs(v + s);
+      }
+#pragma unroll
+      for (int s = 0; s < S; ++s) sum += ex2_approx(x[s] - lse[s]);
+    }
+    tile[kl][lane] = sum * a.mass_scale;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 32 * 32; idx += 256) {
+    const int ql = idx >> 5, kl = idx & 31;
+    if (qb0 + ql < Qb && kb0 + kl < Qb)
+      a.mass[(bh * Qb + qb0 + ql) * Qb + kb0 + kl] = tile[kl][ql];
+  }
+}
+
 template <int LOG2S, bool kRound>
 cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                             cudaStream_t stream) {
@@ -436,7 +526,31 @@ cudaError_t launch_s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArg
                       : launch_log2s_v2<LOG2S, false>(tq, tk, a, stream);
 }
 
+template <int LOG2S>
+cudaError_t launch_reduce_s(const MassArgs& a, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>((a.q_blocks + 31) / 32),
+                  static_cast<unsigned>((a.q_blocks + 31) / 32),
+                  static_cast<unsigned>(a.batch * a.heads));
+  sampled_mass_reduce_kernel<LOG2S><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_sampled_mass_reduce(const MassArgs& a, cudaStream_t stream) {
+  if (a.batch == 0 || a.heads == 0 || a.n_rows == 0) return cudaSuccess;
+  if (a.block_lse == nullptr || a.row_lse == nullptr || a.batch * a.heads > 65535)
+    return cudaErrorInvalidValue;
+  switch (a.samples) {
+    case 1: return launch_reduce_s<0>(a, stream);
+    case 2: return launch_reduce_s<1>(a, stream);
+    case 4: return launch_reduce_s<2>(a, stream);
+    case 8: return launch_reduce_s<3>(a, stream);
+    case 16: return launch_reduce_s<4>(a, stream);
+    case 32: return launch_reduce_s<5>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 cudaError_t launch_sampled_mass(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                                 cudaStream_t stream) {

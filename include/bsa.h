@@ -193,6 +193,27 @@ BSA_API int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64
                      int32_t* err_word, void* stream);
 
 /*
+ * (b) Sampled block mass in one pass over the sampled keys: same inputs,
+ * limits and output as bsa_sampled_mass (within float rounding), plus a
+ * caller workspace of bsa_sampled_mass_workspace_bytes bytes (16-byte
+ * aligned; 1.04 GB for batch 2, 40 heads, 450 blocks, 16 samples).  Each
+ * sampled query row writes the log2 of its exponential sum over every key
+ * block into the workspace as it streams the keys, with its running
+ * stabiliser folded in, and its log-sum-exp at the end; a second kernel then
+ * forms mass = mean over the block's query samples of 2^(block - row).  The
+ * two-pass entry point computes every score twice instead.
+ * Replaces: attention_backends/flex.py:205-251 (_sampled_block_mass).
+ */
+BSA_API int64_t bsa_sampled_mass_workspace_bytes(int64_t batch, int64_t heads, int32_t q_blocks,
+                                                 int32_t samples);
+BSA_API int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_k, int64_t batch,
+                                     int64_t heads, int32_t q_blocks, int32_t samples,
+                                     int32_t head_dim, const float* block_bias, float scale,
+                                     int32_t round_bf16, float* workspace,
+                                     int64_t workspace_bytes, float* mass, int32_t* err_word,
+                                     void* stream);
+
+/*
  * (b) Sampled block mass with no caller workspace; it allocates nothing.
  * No counterpart in the reference: it is bsa_sampled_mass for callers that
  * have no device allocator to take the sampled-row workspace from (a C or C++

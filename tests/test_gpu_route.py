@@ -222,6 +222,26 @@ def test_sampled_mass_480p_matches_reference(golden):
     _native.check_device_errors()
 
 
+@pytest.mark.parametrize("T,block,samples", [(1000, 128, 1), (3000, 128, 2), (4096, 64, 4),
+                                             (2500, 128, 8), (57600, 128, 16), (1900, 64, 32)])
+def test_sampled_mass_one_pass_matches_two_pass(T, block, samples):
+    """One pass over the sampled keys (per-row block log-sums + reduction)
+    against the two-pass kernel, partial last blocks included; rows sum to 1.
+    Both kernels take a quarter of their exponentials from a polynomial with
+    relative error <= 7.5e-5, evaluated at different arguments (running vs
+    final stabiliser), hence rtol 2e-4 (the mass parity bound)."""
+    g = torch.Generator().manual_seed(T + samples)
+    q, k = (torch.randn((2, T, 3, 128), generator=g).to(torch.bfloat16).to(DEV)
+            for _ in range(2))
+    one = kernels.sampled_block_mass(q, k, block, samples)
+    two = kernels.sampled_block_mass(q, k, block, samples, one_pass=False)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    torch.testing.assert_close(one, two, atol=1e-6, rtol=2e-4)
+    rows = one.double().sum(-1)
+    torch.testing.assert_close(rows, torch.ones_like(rows), atol=1e-4, rtol=0)
+
+
 def test_route_decision_config3(golden):
     """Full config 3: mass vs reference, bit-exact selection from the GPU mass."""
     g = golden("config3.npz")
