@@ -241,7 +241,8 @@ int bsa_qkv_prologue(const void* q_proj, const void* k_proj, const void* v_proj,
     return fail(BSA_ERR_INVALID_ARGUMENT, "bad batch/tokens/heads/head_dim (head_dim %% 8 == 0)");
   if ((rope_cos == nullptr) != (rope_sin == nullptr))
     return fail(BSA_ERR_INVALID_ARGUMENT, "rope_cos and rope_sin go together");
-  const void* ptrs[] = {q_proj, k_proj, v_proj, q_out, k_out, v_out, rope_cos, rope_sin};
+  const void* ptrs[] = {q_proj, k_proj, v_proj, q_out, k_out, v_out, rope_cos, rope_sin,
+                        norm_q_weight, norm_k_weight};
   for (const void* p : ptrs)
     if (reinterpret_cast<uintptr_t>(p) & 15)
       return fail(BSA_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");

@@ -36,7 +36,8 @@ __device__ void norm_rope_row(const __nv_bfloat16* __restrict__ src, __nv_bfloat
   const unsigned short* raw = reinterpret_cast<const unsigned short*>(src);
   float r = 1.f;
   if (norm) {
-    const float ss = torch_cpu_sum(
+    // 16 items per lane loaded ahead of their in-order additions
+    const float ss = torch_cpu_sum<16>(
         [raw](int e) {
           const float x = __uint_as_float(static_cast<uint32_t>(__ldg(raw + e)) << 16);
           return __fmul_rn(x, x);
@@ -56,10 +57,17 @@ __device__ void norm_rope_row(const __nv_bfloat16* __restrict__ src, __nv_bfloat
       y[2 * p + 1] = bf16_hi(w[p]);
     }
     if (norm) {
+      float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (weight != nullptr) {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c);
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c + 1);
+        wv[0] = w0.x; wv[1] = w0.y; wv[2] = w0.z; wv[3] = w0.w;
+        wv[4] = w1.x; wv[5] = w1.y; wv[6] = w1.z; wv[7] = w1.w;
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float t = __fmul_rn(y[e], r);
-        if (weight != nullptr) t = __fmul_rn(t, __ldg(weight + c * 8 + e));
+        if (weight != nullptr) t = __fmul_rn(t, wv[e]);
         y[e] = __uint_as_float(bf16_bits(t) << 16);
       }
     }
@@ -101,6 +109,15 @@ __global__ void __launch_bounds__(kPrologueThreads, 4) qkv_prologue_kernel(Prolo
     }
     const int64_t in_off = b * a.in_stride_b + t * a.in_stride_t;
     const int64_t out_off = row * C;
+    if ((threadIdx.x & 31) == 0) {
+      // Whole Q and K rows into L2 at once: the ordered sums below then wait
+      // on L2 rather than DRAM (rows are 16-byte aligned, C * 2 bytes long).
+      const uint32_t bytes = static_cast<uint32_t>(C) * 2u;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.q_in + in_off), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.k_in + in_off), "r"(bytes)
+                   : "memory");
+    }
     const float* cos_t = a.rope_cos != nullptr ? a.rope_cos + t * (a.head_dim / 2) : nullptr;
     const float* sin_t = a.rope_sin != nullptr ? a.rope_sin + t * (a.head_dim / 2) : nullptr;
     norm_rope_row(a.q_in + in_off, a.q_out + out_off, C, a.head_dim, a.norm_q, a.weight_q,

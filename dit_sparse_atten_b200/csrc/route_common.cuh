@@ -26,23 +26,25 @@ __device__ __forceinline__ int ceil_log2(int v) {
   return v <= 1 ? 0 : 32 - __clz(v - 1);
 }
 
-// Cascade over `size` items; item i of this lane is load(index(i)).
-template <typename Load, typename IndexFn>
+// Cascade over `size` items; item i of this lane is load(index(i)).  Items
+// are loaded kBatch at a time ahead of their in-order additions.
+template <int kBatch = 8, typename Load, typename IndexFn>
 __device__ float cascade_sum(Load load, int size, IndexFn index) {
+  static_assert(kBatch == 8 || kBatch == 16, "level_step is a multiple of 16");
   const int level_power = max(4, ceil_log2(size) / 4);
   const int level_step = 1 << level_power;
   const int level_mask = level_step - 1;
   float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
   int i = 0;
   while (i + level_step <= size) {
-    // level_step is a power of two >= 16: items go in groups of 8, all loaded
-    // before any is added (the additions keep their order).
-    for (int j = 0; j < level_step; j += 8, i += 8) {
-      float x[8];
+    // level_step is a power of two >= 16: items go in groups of kBatch, all
+    // loaded before any is added (the additions keep their order).
+    for (int j = 0; j < level_step; j += kBatch, i += kBatch) {
+      float x[kBatch];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] = load(index(i + u));
+      for (int u = 0; u < kBatch; ++u) x[u] = load(index(i + u));
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc0 = __fadd_rn(acc0, x[u]);
+      for (int u = 0; u < kBatch; ++u) acc0 = __fadd_rn(acc0, x[u]);
     }
     acc1 = __fadd_rn(acc1, acc0);
     acc0 = 0.f;
@@ -64,7 +66,7 @@ __device__ float cascade_sum(Load load, int size, IndexFn index) {
 // cascade: lane (k, v) of 4 accumulators x 8 float lanes takes items
 // (4 i + k) * 8 + v, i.e. warp lane k * 8 + v takes items 32 i + lane);
 // executed by one full warp, result valid in every lane.
-template <typename Load>
+template <int kBatch = 8, typename Load>
 __device__ float torch_cpu_sum(Load load, int n) {
   const int lane = threadIdx.x & 31;
   float result = 0.f;
@@ -86,7 +88,7 @@ __device__ float torch_cpu_sum(Load load, int n) {
   const int size_ilp = vec_size / 4;
   const int k = lane >> 3;
   const int v = lane & 7;
-  float acc = cascade_sum(load, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
+  float acc = cascade_sum<kBatch>(load, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
   if (k == 0)
     for (int i = size_ilp * 4; i < vec_size; ++i) acc = __fadd_rn(acc, load(i * 8 + v));
   const float a1 = __shfl_sync(0xffffffffu, acc, (v + 8) & 31);
