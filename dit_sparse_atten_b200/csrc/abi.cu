@@ -396,9 +396,15 @@ int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_k, int64
                                     head_dim, block_bias, scale, round_bf16, mass, err_word, &tq,
                                     &tk, &a);
   if (rc != BSA_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (samples <= 2) {
+    // One or two keys per block: the two-pass kernel (the workspace is unused).
+    cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_onepass launch");
+    return ok();
+  }
   a.block_lse = workspace;
   a.row_lse = workspace + batch * heads * a.n_rows * q_blocks;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, s);
   if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_onepass launch");
   e = bsa::launch_sampled_mass_reduce(a, s);

@@ -47,29 +47,46 @@ struct MassBarriers {
 };
 
 // ---------------------------------------------------------------------------
-// Eight softmax warps, two per SM sub-partition: warp w owns rows 32*(w%4).. and
-// column half w/4 of every S tile, keeps its own running (max, sum) over its
-// half-rows in pass 1 and combines it with the other half once, through
-// shared memory, before pass 2.  All score arithmetic is packed (f32x2); the
-// reference's two bf16 roundings (matmul output, then `* score_scale`) are
-// split between the conversion unit (the first) and the FMA pipe (the second,
-// by Veltkamp splitting), so that neither pipe carries both next to the
-// exponentials; a share of the exponentials runs on the FMA pipe too
-// (exp2_poly2).  For S <= 32 a query block's S rows are S consecutive lanes,
-// reduced with shuffles.  For S = 64, 128 (exact mass) a query block spans
-// several warps: each warp sums its 32 rows with shuffles and writes one
-// partial per key tile into shared memory; every kRedTiles tiles warp 0 adds
-// the eight partials in a fixed order (deterministic) and writes the mass.
-// The hand-over uses mbarriers with bounded waits (red_full / red_free,
-// double-buffered).
-//   warp 8 TMA producer, warp 9 TMEM allocator + tcgen05.mma issuer.
-constexpr int kMass2Threads = 320;
+// Softmax warps (MassShape): warp w owns rows 32*(w%4).. and column part w/4
+// of every S tile (quarters for S <= 32, halves for S = 64, 128), keeps its
+// own running (max, sum) over its part of the row in pass 1 and combines it
+// with the other parts once, through shared memory, before pass 2 (or before
+// writing the row's log-sum-exp in one-pass mode).  All score arithmetic is
+// packed (f32x2); the reference's two bf16 roundings (matmul output, then
+// `* score_scale`) are split between the conversion unit (the first) and the
+// FMA pipe (the second, by Veltkamp splitting), so that neither pipe carries
+// both next to the exponentials; a share of the exponentials runs on the FMA
+// pipe too (exp2_poly2).  For S <= 32 a query block's S rows are S
+// consecutive lanes, reduced with shuffles.  For S = 64, 128 (exact mass) a
+// query block spans several warps: each warp sums its 32 rows with shuffles
+// and writes one partial per key tile into shared memory; every kRedTiles
+// tiles warp 0 adds the eight partials in a fixed order (deterministic) and
+// writes the mass.  The hand-over uses mbarriers with bounded waits
+// (red_full / red_free, double-buffered).  After the softmax warps: the TMA
+// producer warp, then the TMEM allocator + tcgen05.mma issuer warp.
 constexpr int kRedTiles = 16;
 constexpr int kXchgOff = kBiasOff + kMaxBlocks * 4;
-constexpr int kRedOff = kXchgOff + 2 * 128 * 2 * 4;           // [2][kRedTiles][8] floats
+constexpr int kRedOff = kXchgOff + 4 * 128 * 2 * 4;           // [2][kRedTiles][8] floats
 constexpr int kBar2Off = kRedOff + 2 * kRedTiles * 8 * 4;
 constexpr int kMass2Smem = kBar2Off + 256 + 1024;
 constexpr int kMassEmulated = 2;  // of every 8 column pairs, exponentials on the FMA pipe
+
+// Warp layout.  S = 16, 32: sixteen softmax warps, four per SM sub-partition,
+// warp w owning rows 32*(w%4).. and column quarter w/4 of every S tile (more
+// warps to hide the TMEM-load -> exponential -> sum chain; 18 warps cap a
+// thread at 96 registers, which the per-block state of S <= 8 exceeds).
+// Other S: eight softmax warps on column halves.  Then the TMA producer warp
+// and the MMA warp (TMEM allocator).
+template <int LOG2S>
+struct MassShape {
+  static constexpr int kParts = (LOG2S == 4 || LOG2S == 5) ? 4 : 2;  // column parts of a row
+  static constexpr int kSoftWarps = 4 * kParts;
+  static constexpr int kThreads = 32 * kSoftWarps + 64;
+  static constexpr int kProdWarp = kSoftWarps;
+  static constexpr int kMmaWarp = kSoftWarps + 1;
+  static constexpr int kCols = kTile / kParts;          // columns per softmax thread
+  static constexpr int kPairs = kCols / 2;
+};
 
 // bf16 round-to-nearest-even of two floats without the conversion unit:
 // t = x * (2^16 + 1), hi = t - (t - x) keeps the 8 leading significand bits
@@ -101,14 +118,14 @@ __device__ __forceinline__ float2 exp2_pair(float2 t) {
 
 // Log2-domain scores of 64 keys starting at key0 (bias = log(size/S) per key
 // block, keys past n_rows -> -inf), from the raw fp32 accumulators r.
-template <int LOG2S, bool kRound>
+template <int LOG2S, bool kRound, int kPairs>
 __device__ __forceinline__ void mass_scores(const uint32_t* r, float2* y, int64_t key0,
                                             int64_t n_rows, const float* sBiasL, float scale) {
   const float2 sc2 = make_float2(scale, scale);
   const float2 l2e = make_float2(kLog2eM, kLog2eM);
   const int64_t kb0 = key0 >> LOG2S;
 #pragma unroll
-  for (int p = 0; p < 32; ++p) {
+  for (int p = 0; p < kPairs; ++p) {
     float2 v = make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
     if constexpr (kRound) {
       v = round2_bf16(__fmul2_rn(round2_bf16_cvt(v), sc2));
@@ -124,22 +141,57 @@ __device__ __forceinline__ void mass_scores(const uint32_t* r, float2* y, int64_
     }
     y[p] = __ffma2_rn(v, l2e, bl);
   }
-  if (key0 + 64 > n_rows) {
+  if (key0 + 2 * kPairs > n_rows) {
 #pragma unroll
-    for (int p = 0; p < 32; ++p) {
+    for (int p = 0; p < kPairs; ++p) {
       if (key0 + 2 * p >= n_rows) y[p].x = -INFINITY;
       if (key0 + 2 * p + 1 >= n_rows) y[p].y = -INFINITY;
     }
   }
 }
 
+// The reference's rounded and scaled scores of 2 * kPairs keys starting at
+// key0 (keys past n_rows -> -inf), before the log2(e) factor and the block
+// bias: one-pass mode folds both, and its stabiliser, into one FMA per pair.
+template <bool kRound, int kPairs>
+__device__ __forceinline__ void mass_scores_scaled(const uint32_t* r, float2* v, int64_t key0,
+                                                   int64_t n_rows, float scale) {
+  const float2 sc2 = make_float2(scale, scale);
+#pragma unroll
+  for (int p = 0; p < kPairs; ++p) {
+    float2 x = make_float2(__uint_as_float(r[2 * p]), __uint_as_float(r[2 * p + 1]));
+    if constexpr (kRound) {
+      x = round2_bf16(__fmul2_rn(round2_bf16_cvt(x), sc2));
+    } else {
+      x = __fmul2_rn(x, sc2);
+    }
+    v[p] = x;
+  }
+  if (key0 + 2 * kPairs > n_rows) {
+#pragma unroll
+    for (int p = 0; p < kPairs; ++p) {
+      if (key0 + 2 * p >= n_rows) v[p].x = -INFINITY;
+      if (key0 + 2 * p + 1 >= n_rows) v[p].y = -INFINITY;
+    }
+  }
+}
+
+// Of every 8 pairs, exponentials on the FMA pipe in one-pass mode.  Measured
+// at config 4: 0, 1, 2 -> 3.02, 2.97, 2.97 ms; 1 keeps the polynomial's
+// error on the fewest terms.
+constexpr int kOnePassEmulated = 1;
+
 template <int LOG2S, bool kRound>
-__global__ void __launch_bounds__(kMass2Threads, 1)
+__global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
     sampled_mass_kernel2(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k, const MassArgs a) {
   constexpr int S = 1 << LOG2S;
   constexpr bool kWide = S > 32;              // a query block spans several warps
-  constexpr int kHalfBlocks = kWide ? 1 : 64 / S;  // key blocks in a 64-column half tile
+  using Shape = MassShape<LOG2S>;
+  constexpr int kParts = Shape::kParts;
+  constexpr int kCols = Shape::kCols;
+  constexpr int kPairs = Shape::kPairs;
+  constexpr int kPartBlocks = kWide ? 1 : kCols / S;  // key blocks in a part of a tile row
   static_assert(S <= 128, "at most 128 rows per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -147,7 +199,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   uint8_t* sQ = smem;
   uint8_t* sRing = smem + kRingOff;
   float* sBiasL = reinterpret_cast<float*>(smem + kBiasOff);
-  float2* sX = reinterpret_cast<float2*>(smem + kXchgOff);  // [half][row] (max, sum)
+  float2* sX = reinterpret_cast<float2*>(smem + kXchgOff);  // [part][row] (max, sum)
   float* sRed = reinterpret_cast<float*>(smem + kRedOff);    // [buf][tile][warp] (S > 32)
   MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + kBar2Off);
   volatile int* abort_flag = &bar->abort;
@@ -160,7 +212,10 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   const int n_tiles = static_cast<int>((a.n_rows + kTile - 1) / kTile);
   // With the log-sum-exp given, pass 1 is skipped; in one-pass mode pass 1
   // emits per-block log sums and pass 2 is left to the reduction kernel.
-  const bool emit = !kWide && a.block_lse != nullptr;
+  // (S <= 2 has one or two keys per block: the per-block state of one-pass
+  // mode would not fit the registers, so those take two passes.)
+  constexpr bool kOnePass = !kWide && LOG2S >= 2;
+  const bool emit = kOnePass && a.block_lse != nullptr;
   const int pass1 = a.lse != nullptr ? 0 : n_tiles;
   const int steps = emit ? n_tiles : pass1 + n_tiles;
 
@@ -168,7 +223,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
     mbar_init(&bar->q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->s_free[i], 256);
+      mbar_init(&bar->s_free[i], Shape::kSoftWarps * 32);
       mbar_init(&bar->red_full[i], 8);
       mbar_init(&bar->red_free[i], 1);
     }
@@ -182,15 +237,15 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
   }
   __syncthreads();
   if (bar->abort) return;  // uniform: set before the barrier, read after it
-  for (int i = threadIdx.x; i < a.q_blocks; i += kMass2Threads)
+  for (int i = threadIdx.x; i < a.q_blocks; i += Shape::kThreads)
     sBiasL[i] = a.block_bias != nullptr ? a.block_bias[i] * kLog2eM : 0.f;
-  if (warp == 9) tmem_alloc(&bar->tmem_base, 256);
+  if (warp == Shape::kMmaWarp) tmem_alloc(&bar->tmem_base, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
 
-  if (warp == 8) {
+  if (warp == Shape::kProdWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -216,7 +271,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
       for (int s = 0; s < kSlots; ++s)
         if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
-  } else if (warp == 9) {
+  } else if (warp == Shape::kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, kTile, false);
       const uint64_t qdesc = sdesc_sw128(smem_u32(sQ), 16, 1024);
@@ -242,7 +297,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
       mbar_wait(&bar->drain, 0, &never, a.err_word);
     }
   } else {
-    const int half = warp >> 2;
+    const int part = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
@@ -251,7 +306,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
     float m2 = -INFINITY, l = 0.f, m_fold = 0.f;
     if (a.lse != nullptr && qrow < a.n_rows)
       m_fold = a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.n_rows + qrow] * kLog2eM;
-    bool combined = pass1 == 0;   // pass 1's two half-rows met (named barrier 1 + wq)
+    bool combined = pass1 == 0;   // pass 1's row parts met (named barrier 1 + wq)
     bool ok = true;
     for (int i = 0; i < steps; ++i) {
       if (!mbar_wait(&bar->s_full[i & 1], (i >> 1) & 1, abort_flag, a.err_word)) {
@@ -259,68 +314,90 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[64];
-      tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + half * 64, r);
-      tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + half * 64 + 32, r + 32);
+      uint32_t r[kCols];
+#pragma unroll
+      for (int c = 0; c < kCols; c += 32)
+        tmem_ld_32x32b_x32(tmem + lane_addr + (i & 1) * 128 + part * kCols + c, r + c);
       tmem_wait_ld();
-      reg_fence<64>(r);
+      reg_fence<kCols>(r);
       tc_fence_before();
       mbar_arrive(&bar->s_free[i & 1]);
-      const int64_t key0 = static_cast<int64_t>(i % n_tiles) * kTile + half * 64;
-      float2 y[32];
-      mass_scores<LOG2S, kRound>(r, y, key0, a.n_rows, sBiasL, a.scale);
-      if (i < pass1) {
-        // Pass 1: running max and sum of this half-row.
+      const int64_t key0 = static_cast<int64_t>(i % n_tiles) * kTile + part * kCols;
+      if (kOnePass && emit) {
+        // One pass.  Stabiliser: the running max of (score * log2 e + the
+        // largest block bias of this part), an upper bound of every argument,
+        // so each exponential's argument is a single FMA with a per-block
+        // constant (bias - m).
+        float2 v[kPairs];
+        mass_scores_scaled<kRound, kPairs>(r, v, key0, a.n_rows, a.scale);
+        const int64_t kb0 = key0 >> LOG2S;
+        // Block kb0 + gi covers pairs [gi * S / 2, (gi + 1) * S / 2) of this
+        // part.
+        auto bias = [&](int gi) { return kb0 + gi < a.q_blocks ? sBiasL[kb0 + gi] : 0.f; };
+        float bmax = -INFINITY;
+#pragma unroll
+        for (int gi = 0; gi < kPartBlocks; ++gi)
+          if (kb0 + gi < a.q_blocks) bmax = fmaxf(bmax, sBiasL[kb0 + gi]);
+        float m8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) m8[q] = fmaxf(v[q].x, v[q].y);
+#pragma unroll
+        for (int p = 8; p < kPairs; p += 8) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) m8[q] = fmax3(m8[q], v[p + q].x, v[p + q].y);
+        }
+        const float vmax = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
+                                 fmaxf(m8[6], m8[7]));
+        const float m_tile = vmax == -INFINITY ? -INFINITY : __fmaf_rn(vmax, kLog2eM, bmax);
+        const float m_new = fmaxf(m2, m_tile);
+        if (m_new != -INFINITY) {
+          const float2 l2e = make_float2(kLog2eM, kLog2eM);
+          float* dst = a.block_lse + (out_rows + kb0) * a.n_rows + qrow;
+          const bool write = qrow < a.n_rows;
+          float tot = 0.f;
+          constexpr int kBlockPairs = S / 2;
+#pragma unroll
+          for (int gi = 0; gi < kPartBlocks; ++gi) {
+            const float c = __fsub_rn(bias(gi), m_new);
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < kBlockPairs; ++u) {
+              const int p = gi * kBlockPairs + u;
+              const float2 t = __ffma2_rn(v[p], l2e, make_float2(c, c));
+              const float2 e =
+                  (p & 7) >= 8 - kOnePassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
+              acc = __fadd2_rn(acc, e);
+            }
+            const float g = acc.x + acc.y;
+            tot += g;
+            if (write && kb0 + gi < a.q_blocks) dst[gi * a.n_rows] = m_new + __log2f(g);
+          }
+          l = l * ex2_approx(m2 - m_new) + tot;
+          m2 = m_new;
+        }
+      } else if (i < pass1) {
+        float2 y[kPairs];
+        mass_scores<LOG2S, kRound, kPairs>(r, y, key0, a.n_rows, sBiasL, a.scale);
+        // Pass 1: running max and sum of this part of the row.
         float m8[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) m8[q] = fmaxf(y[q].x, y[q].y);
 #pragma unroll
-        for (int p = 8; p < 32; p += 8) {
+        for (int p = 8; p < kPairs; p += 8) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) m8[q] = fmax3(m8[q], y[p + q].x, y[p + q].y);
         }
         const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]),
                                fmaxf(m8[6], m8[7]));
         const float m_new = fmaxf(m2, mx);
-        // A half-row whose keys so far are all past the sequence (few sampled
-        // rows) keeps (-inf, 0): -inf - -inf would be NaN.  Its blocks are
-        // all past the sequence too, so one-pass mode has nothing to write.
-        if (emit && m_new != -INFINITY) {
-          // One pass: exponentials summed per key block, relative to m_new;
-          // each block's log2 sum (absolute) goes to the workspace.
-          const float2 nm = make_float2(-m_new, -m_new);
-          float g[kHalfBlocks];
-#pragma unroll
-          for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
-#pragma unroll
-          for (int p = 0; p < 32; ++p) {
-            const float2 t = __fadd2_rn(y[p], nm);
-            const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
-            if constexpr (LOG2S == 0) {
-              g[2 * p] += e.x;
-              g[2 * p + 1] += e.y;
-            } else {
-              g[(2 * p) >> LOG2S] += e.x + e.y;
-            }
-          }
-          float tot = 0.f;
-#pragma unroll
-          for (int gi = 0; gi < kHalfBlocks; ++gi) tot += g[gi];
-          l = l * ex2_approx(m2 - m_new) + tot;
-          m2 = m_new;
-          if (qrow < a.n_rows) {
-            const int64_t kb0 = key0 >> LOG2S;
-            float* dst = a.block_lse + (out_rows + kb0) * a.n_rows + qrow;
-#pragma unroll
-            for (int gi = 0; gi < kHalfBlocks; ++gi)
-              if (kb0 + gi < a.q_blocks) dst[gi * a.n_rows] = m_new + __log2f(g[gi]);
-          }
-        } else if (m_new != -INFINITY) {
+        // A row part whose keys so far are all past the sequence (few sampled
+        // rows) keeps (-inf, 0): -inf - -inf would be NaN.
+        if (m_new != -INFINITY) {
           const float2 nm = make_float2(-m_new, -m_new);
           float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                            make_float2(0.f, 0.f)};
 #pragma unroll
-          for (int p = 0; p < 32; ++p) {
+          for (int p = 0; p < kPairs; ++p) {
             const float2 t = __fadd2_rn(y[p], nm);
             const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
             acc[p & 3] = __fadd2_rn(acc[p & 3], e);
@@ -329,29 +406,47 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
           l = l * ex2_approx(m2 - m_new) + (a03.x + a03.y);
           m2 = m_new;
         }
-        if (i == n_tiles - 1) {
-          // Combine with the other half-row: both warps of these rows meet at
-          // named barrier 1 + wq.
-          sX[half * 128 + row] = make_float2(m2, l);
-          asm volatile("bar.sync %0, 64;" ::"r"(1 + wq) : "memory");
+      }
+      if ((emit || i < pass1) && i == n_tiles - 1) {
+        {
+          // End of the pass over the keys.  Combine the row's parts: the warps of these rows meet at named
+          // barrier 1 + wq; every part adds the partial sums in part order.
+          sX[part * 128 + row] = make_float2(m2, l);
+          asm volatile("bar.sync %0, %1;" ::"r"(1 + wq), "r"(32 * kParts) : "memory");
           combined = true;
-          const float2 o = sX[(half ^ 1) * 128 + row];
-          const float m_all = fmaxf(m2, o.x);
-          const float l_all = l * ex2_approx(m2 - m_all) + o.y * ex2_approx(o.x - m_all);
+          float m_all, l_all;
+          if constexpr (kParts == 2) {
+            const float2 o = sX[(part ^ 1) * 128 + row];
+            m_all = fmaxf(m2, o.x);
+            l_all = l * ex2_approx(m2 - m_all) + o.y * ex2_approx(o.x - m_all);
+          } else {
+            float2 o[kParts];
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) o[q] = sX[q * 128 + row];
+            m_all = o[0].x;
+#pragma unroll
+            for (int q = 1; q < kParts; ++q) m_all = fmaxf(m_all, o[q].x);
+            l_all = o[0].y * ex2_approx(o[0].x - m_all);
+#pragma unroll
+            for (int q = 1; q < kParts; ++q) l_all += o[q].y * ex2_approx(o[q].x - m_all);
+          }
           // 2^(y - m_fold) = 2^(y - m_all) / l_all
           m_fold = m_all + __log2f(l_all);
-          if (emit && half == 0 && qrow < a.n_rows)
+          if (emit && part == 0 && qrow < a.n_rows)
             a.row_lse[(static_cast<int64_t>(b) * a.heads + h) * a.n_rows + qrow] = m_fold;
         }
-      } else {
+      }
+      if (!emit && i >= pass1) {
         // Pass 2: normalised probabilities summed per key block, then over the
         // S sampled rows of each query block.
+        float2 y[kPairs];
+        mass_scores<LOG2S, kRound, kPairs>(r, y, key0, a.n_rows, sBiasL, a.scale);
         const float2 nf = make_float2(-m_fold, -m_fold);
-        float g[kHalfBlocks];
+        float g[kPartBlocks];
 #pragma unroll
-        for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
+        for (int gi = 0; gi < kPartBlocks; ++gi) g[gi] = 0.f;
 #pragma unroll
-        for (int p = 0; p < 32; ++p) {
+        for (int p = 0; p < kPairs; ++p) {
           const float2 t = __fadd2_rn(y[p], nf);
           const float2 e = (p & 7) >= 8 - kMassEmulated ? exp2_pair<1>(t) : exp2_pair<0>(t);
           if constexpr (LOG2S == 0) {
@@ -363,12 +458,12 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
         }
         if (qrow >= a.n_rows) {
 #pragma unroll
-          for (int gi = 0; gi < kHalfBlocks; ++gi) g[gi] = 0.f;
+          for (int gi = 0; gi < kPartBlocks; ++gi) g[gi] = 0.f;
         }
         if constexpr (!kWide) {
           if constexpr (S > 1) {
 #pragma unroll
-            for (int gi = 0; gi < kHalfBlocks; ++gi) {
+            for (int gi = 0; gi < kPartBlocks; ++gi) {
 #pragma unroll
               for (int off = 1; off < S; off <<= 1)
                 g[gi] += __shfl_xor_sync(0xffffffffu, g[gi], off);
@@ -379,7 +474,7 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
           if ((lane & (S - 1)) == 0 && qblock < a.q_blocks) {
             float* dst = a.mass + (out_rows + qblock) * a.q_blocks;
 #pragma unroll
-            for (int gi = 0; gi < kHalfBlocks; ++gi)
+            for (int gi = 0; gi < kPartBlocks; ++gi)
               if (kb0 + gi < a.q_blocks) dst[kb0 + gi] = g[gi] * a.mass_scale;
           }
         } else {
@@ -433,13 +528,13 @@ __global__ void __launch_bounds__(kMass2Threads, 1)
       }
     }
     // A warp that left pass 1 early (a timed-out wait) still arrives at the
-    // half-row barrier, so that the other warp of these rows is not held there.
-    if (!combined) asm volatile("bar.arrive %0, 64;" ::"r"(1 + wq) : "memory");
+    // row-part barrier, so that the other warps of these rows are not held there.
+    if (!combined) asm volatile("bar.arrive %0, %1;" ::"r"(1 + wq), "r"(32 * kParts) : "memory");
     (void)ok;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == Shape::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
@@ -515,7 +610,8 @@ cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const 
   }
   const dim3 grid(static_cast<unsigned>((a.n_rows + kTile - 1) / kTile),
                   static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  sampled_mass_kernel2<LOG2S, kRound><<<grid, kMass2Threads, kMass2Smem, stream>>>(tq, tk, a);
+  sampled_mass_kernel2<LOG2S, kRound>
+      <<<grid, MassShape<LOG2S>::kThreads, kMass2Smem, stream>>>(tq, tk, a);
   return cudaGetLastError();
 }
 

@@ -201,7 +201,8 @@ BSA_API int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64
  * block into the workspace as it streams the keys, with its running
  * stabiliser folded in, and its log-sum-exp at the end; a second kernel then
  * forms mass = mean over the block's query samples of 2^(block - row).  The
- * two-pass entry point computes every score twice instead.
+ * two-pass entry point computes every score twice instead; samples <= 2
+ * (one or two keys per block) take that kernel here too, workspace unused.
  * Replaces: attention_backends/flex.py:205-251 (_sampled_block_mass).
  */
 BSA_API int64_t bsa_sampled_mass_workspace_bytes(int64_t batch, int64_t heads, int32_t q_blocks,
