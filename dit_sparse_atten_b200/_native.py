@@ -40,6 +40,9 @@ SIGNATURES = {
     "bsa_exact_block_mass": ([_P, _P, _I64, _I64, _I64, _I32, _I32, _F32, _P, _P, _P, _P], _I32),
     "bsa_attention_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _P, _P, _I32,
                            _I32, _I32, _F32, _P, _I64, _I64, _I64, _P, _P, _P], _I32),
+    "bsa_attention_fwd_scatter": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _P, _P,
+                                   _I32, _I32, _I32, _F32, _P, _P, _I64, _I64, _I64, _P, _P, _P],
+                                  _I32),
     "bsa_attention_dense_block_mass": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64,
                                         _F32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], _I32),
     "bsa_exp2": ([_P, _P, _I64, _I32, _P], _I32),

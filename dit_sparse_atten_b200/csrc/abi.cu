@@ -550,7 +550,8 @@ static int attention_launch(const char* name, const void* q, const void* k, cons
                             const int32_t* counts, const int32_t* indices, int32_t route_cols,
                             int32_t route_has_batch, int32_t block, float scale, void* out,
                             int64_t out_stride_b, int64_t out_stride_t, int64_t out_stride_h,
-                            float* lse, float* block_lse, int32_t* err_word, void* stream) {
+                            float* lse, float* block_lse, int32_t* err_word, void* stream,
+                            const int32_t* out_rows = nullptr) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || counts == nullptr ||
       indices == nullptr || err_word == nullptr)
     return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
@@ -602,6 +603,7 @@ static int attention_launch(const char* name, const void* q, const void* k, cons
   a.lse = lse;
   a.err_word = err_word;
   a.block_lse = block_lse;
+  a.out_rows = out_rows;
   cudaError_t e = bsa::launch_attention(tq, tk, tv, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);
   return ok();
@@ -617,6 +619,23 @@ int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
                           in_stride_b, in_stride_t, in_stride_h, counts, indices, route_cols,
                           route_has_batch, block, scale, out, out_stride_b, out_stride_t,
                           out_stride_h, lse, nullptr, err_word, stream);
+}
+
+int bsa_attention_fwd_scatter(const void* q, const void* k, const void* v, int64_t batch,
+                              int64_t tokens, int64_t heads, int32_t head_dim,
+                              int64_t in_stride_b, int64_t in_stride_t, int64_t in_stride_h,
+                              const int32_t* counts, const int32_t* indices, int32_t route_cols,
+                              int32_t route_has_batch, int32_t block, float scale,
+                              const int32_t* out_rows, void* out, int64_t out_stride_b,
+                              int64_t out_stride_t, int64_t out_stride_h, float* lse,
+                              int32_t* err_word, void* stream) {
+  if (out_rows == nullptr) return fail(BSA_ERR_INVALID_ARGUMENT, "out_rows is null");
+  if (out == q || out == k || out == v)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "out must not alias q, k or v (rows are permuted)");
+  return attention_launch("bsa_attention_fwd_scatter launch", q, k, v, batch, tokens, heads,
+                          head_dim, in_stride_b, in_stride_t, in_stride_h, counts, indices,
+                          route_cols, route_has_batch, block, scale, out, out_stride_b,
+                          out_stride_t, out_stride_h, lse, nullptr, err_word, stream, out_rows);
 }
 
 int bsa_attention_dense_block_mass(const void* q, const void* k, const void* v, int64_t batch,

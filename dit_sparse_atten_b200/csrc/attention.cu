@@ -505,9 +505,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                      a.err_word);
       tc_fence_after();
     }
+    // Destination token of this row (the unpack folded into the store).
+    int64_t out_token = token;
+    bool row_store = row_valid;
+    if (a.out_rows != nullptr && row_valid) {
+      out_token = __ldg(a.out_rows + token);
+      if (out_token < 0 || out_token >= a.tokens) {
+        atomicOr(a.err_word, kErrBadRoute);
+        row_store = false;
+      }
+    }
     if (warp_active) {
-      __nv_bfloat16* out =
-          a.out + b * a.out_stride_b + token * a.out_stride_t + h * a.out_stride_h + grp * 64;
+      __nv_bfloat16* out = a.out + b * a.out_stride_b + out_token * a.out_stride_t +
+                           h * a.out_stride_h + grp * 64;
       const float inv_l = (n > 0 && l_row > 0.f) ? 1.f / l_row : 0.f;
 #pragma unroll 1
       for (int cc = 0; cc < kHeadDim / 64; ++cc) {
@@ -520,7 +530,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int x = 0; x < 32; ++x) o[x] = 0u;
         }
-        if (row_valid) {
+        if (row_store) {
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
             uint4 pk;

@@ -144,8 +144,12 @@ struct AttnArgs {
   float scale;
   __nv_bfloat16* out;             // [B, T, H, D] with strides below (elements)
   int64_t out_stride_b, out_stride_t, out_stride_h;
-  float* lse;                     // [B, H, T] or nullptr
+  float* lse;                     // [B, H, T] or nullptr (packed row order)
   int* err_word;
+  // Output row of each packed query row: row i of every batch element goes
+  // to token out_rows[i] of out (the reorder's permutation, folding the
+  // unpack into the epilogue); nullptr writes row i to token i.
+  const int32_t* out_rows;
   // Dense attention with block mass: non-null selects every key block in
   // order (counts / indices unused) and receives [B, H, Kb, T] per-row,
   // per-key-block log2 exponential sums (block == 128).

@@ -74,66 +74,68 @@ __global__ void __launch_bounds__(kCellThreads) frontier_kernel(const uint8_t* _
                                                                 int64_t planes, int n,
                                                                 uint8_t* __restrict__ out,
                                                                 int* err_word) {
-  const int64_t cells = planes * n * static_cast<int64_t>(n);
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(kCellThreads) + threadIdx.x; c < cells;
-       c += static_cast<int64_t>(gridDim.x) * kCellThreads) {
-    const int k = static_cast<int>(c % n);
-    const int64_t pq = c / n;
+  // One CTA per (plane, q) row at a time, threads across k: the row's
+  // coordinates and Q neighbours are computed once per row, not per cell.
+  const int64_t rows = planes * n;
+  for (int64_t pq = blockIdx.x; pq < rows; pq += gridDim.x) {
     const int q = static_cast<int>(pq % n);
-    const uint8_t* plane = route + (pq / n) * n * static_cast<int64_t>(n);
+    const uint8_t* plane = route + (pq - q) * n;
     const int4 nq = load_neighbors(nb, q, n, err_word);
-    const int4 nk = load_neighbors(nb, k, n, err_word);
-    out[c] = on_frontier(plane, n, q, k, nq, nk) ? 1 : 0;
+    for (int k = threadIdx.x; k < n; k += kCellThreads) {
+      const int4 nk = load_neighbors(nb, k, n, err_word);
+      out[pq * n + k] = on_frontier(plane, n, q, k, nq, nk) ? 1 : 0;
+    }
   }
 }
 
 __global__ void __launch_bounds__(kCellThreads) candidate_scatter_kernel(DirectionalArgs a) {
   const int n = a.n;
-  const int64_t nn = static_cast<int64_t>(n) * n;
-  const int64_t cells = a.planes * nn;
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(kCellThreads) + threadIdx.x; c < cells;
-       c += static_cast<int64_t>(gridDim.x) * kCellThreads) {
-    const int k = static_cast<int>(c % n);
-    const int64_t pq = c / n;
+  // One CTA per (plane, q) row at a time, threads across k (no per-cell
+  // divisions; the row's Q neighbours are loaded once).
+  const int64_t rows = a.planes * n;
+  for (int64_t pq = blockIdx.x; pq < rows; pq += gridDim.x) {
     const int q = static_cast<int>(pq % n);
-    const int64_t p0 = (pq / n) * nn;
+    const int64_t p0 = (pq - q) * n;
     const uint8_t* prev = a.prev + p0;
     const float* mass = a.mass + p0;
     const int4 nq = load_neighbors(a.neighbors, q, n, a.err_word);
-    const int4 nk = load_neighbors(a.neighbors, k, n, a.err_word);
-    const bool front = a.prev_frontier != nullptr ? a.prev_frontier[c] != 0
-                                                  : on_frontier(prev, n, q, k, nq, nk);
-    if (!front) continue;
-    const float floor_value = __fmul_rn(mass[static_cast<size_t>(q) * n + k], a.min_ratio);
-    // Along Q: neighbour rows t of this column; along K: neighbour columns t
-    // of this row.  A neighbour counts when it exists and is unselected;
-    // the first of equal maxima wins.
-    float best_q = -INFINITY, best_k = -INFINITY;
-    int tgt_q = max(nq.x, 0), tgt_k = max(nk.x, 0);
+    for (int k = threadIdx.x; k < n; k += kCellThreads) {
+      const int64_t c = pq * n + k;
+      const int4 nk = load_neighbors(a.neighbors, k, n, a.err_word);
+      const bool front = a.prev_frontier != nullptr ? a.prev_frontier[c] != 0
+                                                    : on_frontier(prev, n, q, k, nq, nk);
+      if (!front) continue;
+      const float floor_value = __fmul_rn(mass[static_cast<size_t>(q) * n + k], a.min_ratio);
+      // Along Q: neighbour rows t of this column; along K: neighbour columns t
+      // of this row.  A neighbour counts when it exists and is unselected;
+      // the first of equal maxima wins.
+      float best_q = -INFINITY, best_k = -INFINITY;
+      int tgt_q = max(nq.x, 0), tgt_k = max(nk.x, 0);
 #pragma unroll
-    for (int d = 0; d < 4; ++d) {
-      const int tq = nb_at(nq, d);
-      const float vq = (tq >= 0 && !prev[static_cast<size_t>(tq) * n + k])
-                           ? mass[static_cast<size_t>(tq) * n + k] : -INFINITY;
-      if (d == 0 || vq > best_q) {
-        if (d != 0) tgt_q = tq;
-        best_q = vq;
+      for (int d = 0; d < 4; ++d) {
+        const int tq = nb_at(nq, d);
+        const float vq = (tq >= 0 && !prev[static_cast<size_t>(tq) * n + k])
+                             ? mass[static_cast<size_t>(tq) * n + k] : -INFINITY;
+        if (d == 0 || vq > best_q) {
+          if (d != 0) tgt_q = tq;
+          best_q = vq;
+        }
+        const int tk = nb_at(nk, d);
+        const float vk = (tk >= 0 && !prev[static_cast<size_t>(q) * n + tk])
+                             ? mass[static_cast<size_t>(q) * n + tk] : -INFINITY;
+        if (d == 0 || vk > best_k) {
+          if (d != 0) tgt_k = tk;
+          best_k = vk;
+        }
       }
-      const int tk = nb_at(nk, d);
-      const float vk = (tk >= 0 && !prev[static_cast<size_t>(q) * n + tk])
-                           ? mass[static_cast<size_t>(q) * n + tk] : -INFINITY;
-      if (d == 0 || vk > best_k) {
-        if (d != 0) tgt_k = tk;
-        best_k = vk;
-      }
+      const bool elig_q = isfinite(best_q) && best_q >= floor_value;
+      const bool elig_k = isfinite(best_k) && best_k >= floor_value;
+      uint8_t* cand = a.candidates + p0;
+      if ((a.expand & kExpandQ) && elig_q) cand[static_cast<size_t>(tgt_q) * n + k] = 1;
+      if ((a.expand & kExpandK) && elig_k) cand[static_cast<size_t>(q) * n + tgt_k] = 1;
+      if ((a.expand & kExpandJoint) && elig_q && elig_k)
+        cand[static_cast<size_t>(tgt_q) * n + tgt_k] = 1;
     }
-    const bool elig_q = isfinite(best_q) && best_q >= floor_value;
-    const bool elig_k = isfinite(best_k) && best_k >= floor_value;
-    uint8_t* cand = a.candidates + p0;
-    if ((a.expand & kExpandQ) && elig_q) cand[static_cast<size_t>(tgt_q) * n + k] = 1;
-    if ((a.expand & kExpandK) && elig_k) cand[static_cast<size_t>(q) * n + tgt_k] = 1;
-    if ((a.expand & kExpandJoint) && elig_q && elig_k)
-      cand[static_cast<size_t>(tgt_q) * n + tgt_k] = 1;
   }
 }
 
@@ -327,10 +329,10 @@ cudaError_t launch_directional_warp(const DirectionalArgs& a, int64_t rows, cuda
   return cudaGetLastError();
 }
 
-unsigned cell_grid(int64_t cells, int num_sms) {
-  const int64_t want = (cells + kCellThreads - 1) / kCellThreads;
+// Row-strided grid: one CTA per (plane, q) row, at most 8 CTAs per SM.
+unsigned row_grid(int64_t rows, int num_sms) {
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
-  return static_cast<unsigned>(want < cap ? (want > 0 ? want : 1) : cap);
+  return static_cast<unsigned>(rows < cap ? (rows > 0 ? rows : 1) : cap);
 }
 
 }  // namespace
@@ -340,7 +342,7 @@ cudaError_t launch_frontier_mask(const uint8_t* route, const int32_t* neighbors,
                                  cudaStream_t stream, int num_sms) {
   const int64_t cells = planes * n * static_cast<int64_t>(n);
   if (cells == 0) return cudaSuccess;
-  frontier_kernel<<<cell_grid(cells, num_sms), kCellThreads, 0, stream>>>(route, neighbors, planes,
+  frontier_kernel<<<row_grid(planes * n, num_sms), kCellThreads, 0, stream>>>(route, neighbors, planes,
                                                                           n, frontier, err_word);
   return cudaGetLastError();
 }
@@ -350,7 +352,7 @@ cudaError_t launch_directional_update(const DirectionalArgs& a, cudaStream_t str
   const int64_t rows = a.planes * a.n;
   if (rows == 0) return cudaSuccess;
   if (a.n <= 0 || a.n > kMaxCols) return cudaErrorInvalidValue;
-  candidate_scatter_kernel<<<cell_grid(rows * a.n, num_sms), kCellThreads, 0, stream>>>(a);
+  candidate_scatter_kernel<<<row_grid(rows, num_sms), kCellThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (a.n <= 32) return launch_directional_warp<1>(a, rows, stream);

@@ -125,14 +125,20 @@ def _build_block_mask(route, tokens, block_size):
     return BlockRoute(counts, indices, tokens, block_size)
 
 
-def _flex_output(q, k, v, block_mask, block_size, compile_kernel=True, scale=None):
-    """Block-sparse attention of ``[B, T, H, D]`` tensors over a CSR route."""
+def _flex_output(q, k, v, block_mask, block_size, compile_kernel=True, scale=None,
+                 out_rows=None):
+    """Block-sparse attention of ``[B, T, H, D]`` tensors over a CSR route.
+
+    With ``out_rows`` (the spatial layout's permutation) the output rows are
+    stored straight back to raster order (the unpack folded into the store).
+    """
     del compile_kernel
     counts = block_mask.counts
     indices = block_mask.indices
     if counts.dim() == 3 and counts.shape[0] == 1:
         counts, indices = counts[0], indices[0]
-    return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size, scale=scale)
+    return kernels.block_sparse_attention(q, k, v, counts, indices, block=block_size, scale=scale,
+                                          out_rows=out_rows)
 
 
 def _dense_and_mass(q, k, v, block_size, scale=None):
@@ -582,15 +588,18 @@ class FlexReuseBackend:
                 self.phase_counts["dense_dispatch"] += 1
                 return finish(self.dense(q, k, v, **dense_only))
 
+        # The sparse output goes straight back to raster order (no unpack pass).
         output = _flex_output(q, k, v, state["block_mask"], self.config.block_size,
-                              self.config.compile_kernel, scale=softmax_scale)
+                              self.config.compile_kernel, scale=softmax_scale,
+                              out_rows=layout.permutation(q.device) if layout is not None
+                              else None)
         self.phase_counts["sparse_reuse"] += 1
         if self.config.prefetch_sampled_update and sampled_update_due:
             state["block_mask"] = None
             self._prefetch_sampled_route(state, q, k, step, softmax_scale)
         if self._is_final_step(step):
             self._release_route(key, state)
-        return finish(output)
+        return output.to(output_dtype)
 
 
 def install_flex_reuse(config=None):

@@ -450,13 +450,17 @@ def dense_attention_block_mass(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
 def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            counts: torch.Tensor, indices: torch.Tensor, block: int = 128,
                            scale: float | None = None, out: torch.Tensor | None = None,
-                           return_lse: bool = False):
+                           return_lse: bool = False, out_rows: torch.Tensor | None = None):
     """Block-sparse attention over a CSR route.
 
     ``q, k, v``: bf16 ``[B, T, H, D]``.  ``counts``: int32 ``[H, Qb]`` (one route
     for every batch element) or ``[B, H, Qb]``; ``indices``: int32 with a trailing
     ``route_cols >= Qb`` axis.  Returns bf16 ``[B, T, H, D]`` (and fp32 LSE
     ``[B, H, T]`` when ``return_lse``).  Reference ``flex.py:358-399``.
+    ``out_rows`` (int32 ``[T]`` permutation on q's device): row i is written to
+    token ``out_rows[i]`` of the output (``bsa_attention_fwd_scatter``), e.g. the
+    spatial layout's pack permutation to get the output back in raster order
+    without an unpack pass; the LSE stays in q's row order.
     """
     device = _require_cuda(q, k, v, counts, indices)
     if not (q.shape == k.shape == v.shape) or q.dim() != 4:
@@ -489,6 +493,17 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     lse = torch.empty((B, H, T), dtype=torch.float32, device=device) if return_lse else None
     s = float(scale) if scale is not None else D ** -0.5
     ost = out.stride()
+    if out_rows is not None:
+        if (out_rows.dtype != torch.int32 or out_rows.shape != (T,)
+                or out_rows.device != q.device):
+            raise ValueError("out_rows must be int32 [T] on q's device")
+        out_rows = out_rows.contiguous()
+        _native.call("bsa_attention_fwd_scatter", q.data_ptr(), k.data_ptr(), v.data_ptr(), B,
+                     T, H, D, q.stride(0), q.stride(1), q.stride(2), counts.data_ptr(),
+                     indices.data_ptr(), indices.shape[-1], has_batch, block, s,
+                     out_rows.data_ptr(), out.data_ptr(), ost[0], ost[1], ost[2],
+                     _native.ptr(lse), _native.err_word(device).data_ptr(), _stream(device))
+        return (out, lse) if return_lse else out
     _native.call("bsa_attention_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), B, T, H, D,
                  q.stride(0), q.stride(1), q.stride(2), counts.data_ptr(), indices.data_ptr(),
                  indices.shape[-1], has_batch, block, s, out.data_ptr(), ost[0], ost[1], ost[2],

@@ -100,6 +100,11 @@ class SpatialTokenLayout:
     def neighbors(self, device):
         return self._device_values(device)[2]
 
+    def permutation(self, device):
+        """int32 ``[T]`` on ``device``: packed row i holds token ``permutation[i]``
+        (also the output rows of the attention's folded unpack)."""
+        return self._device_values(device)[0]
+
 
 def build_spatial_layout(grid, block_size=128, max_microtile_tokens=32):
     """Reversible Morton-ordered packing with no padding (``spatial.py:99-183``)."""
@@ -200,6 +205,10 @@ class TileMajorLayout:
 
     def restore(self, tensor):
         return kernels.reorder_rows([tensor], self._device_values(tensor.device)[1])[0]
+
+    def permutation(self, device):
+        """int32 ``[T]`` on ``device``: tile-major row i holds token ``permutation[i]``."""
+        return self._device_values(device)[0]
 
 
 def tile_major_layout(grid, tile_h, tile_w):

@@ -274,6 +274,29 @@ BSA_API int bsa_attention_fwd(const void* q, const void* k, const void* v, int64
                       int64_t out_stride_h, float* lse, int32_t* err_word, void* stream);
 
 /*
+ * (a) Block-sparse attention forward with the spatial unpack folded into the
+ * output store: the same arguments as bsa_attention_fwd, plus out_rows
+ * (int32 [tokens], a permutation): query row i (in the packed route-block
+ * order of q, k and v) of every batch element is written to token out_rows[i]
+ * of out.  With out_rows = the layout's pack permutation the output comes out
+ * in the original (F, H, W) token order, so no separate unpack pass is needed.
+ * out must not alias q, k or v.  lse, when given, stays in packed row order.
+ * Ids outside [0, tokens) set BSA_DEVICE_BAD_ROUTE and their rows are not
+ * written.
+ * Replaces: attention_backends/flex.py:358-399 (_flex_output) followed by the
+ *           output restore of flex.py:694-700 / spatial.py:86-93.
+ */
+BSA_API int bsa_attention_fwd_scatter(const void* q, const void* k, const void* v, int64_t batch,
+                                      int64_t tokens, int64_t heads, int32_t head_dim,
+                                      int64_t in_stride_b, int64_t in_stride_t,
+                                      int64_t in_stride_h, const int32_t* counts,
+                                      const int32_t* indices, int32_t route_cols,
+                                      int32_t route_has_batch, int32_t block, float scale,
+                                      const int32_t* out_rows, void* out, int64_t out_stride_b,
+                                      int64_t out_stride_t, int64_t out_stride_h, float* lse,
+                                      int32_t* err_word, void* stream);
+
+/*
  * Diagnostics: y[i] = 2^x[i] for n float32 values through one of the two
  * exponential paths of the softmax kernels: mode 0 = the MUFU ex2.approx
  * instruction, mode 1 = the FMA-pipe polynomial (Cody-Waite split + Remez

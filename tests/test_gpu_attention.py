@@ -198,3 +198,50 @@ def test_exp2_paths_accuracy():
     assert (np.abs(poly - cuda_exp2f) / cuda_exp2f)[normal].max() <= 1e-4 + 2.0 ** -22
     below = kernels.exp2(torch.tensor([-200.0, -1000.0], device=DEV), "poly").cpu()
     assert (below >= 0).all() and (below < 2.0 ** -125).all()
+
+
+@pytest.mark.parametrize("grid,block,batch,heads", [((2, 16, 32), 128, 2, 3),
+                                                    ((3, 8, 16), 64, 1, 2),
+                                                    ((5, 30, 52), 128, 2, 2)])
+def test_scatter_store_equals_attention_then_restore(grid, block, batch, heads):
+    """The unpack folded into the output store (bsa_attention_fwd_scatter) is
+    bit-identical to attention in packed order followed by the layout's
+    restore, partial last blocks (5x30x52 = 7,800 tokens) and batch included."""
+    lay = build_spatial_layout(grid, block)
+    tokens = grid[0] * grid[1] * grid[2]
+    blocks = math.ceil(tokens / block)
+    g = torch.Generator().manual_seed(tokens + heads)
+    q, k, v = (torch.randn((batch, tokens, heads, 128), generator=g).to(torch.bfloat16).to(DEV)
+               for _ in range(3))
+    route = torch.rand((heads, blocks, blocks), generator=g) < 0.55
+    route[:, :, 0] = True
+    counts, indices = kernels.pack_boolean_rows(route.to(DEV))
+    qp, kp, vp = lay.reorder_qkv(q, k, v)
+    ref = lay.restore(kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=block))
+    perm = lay.permutation_cpu.to(DEV)
+    got, lse = kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=block,
+                                              out_rows=perm, return_lse=True)
+    _, lse_ref = kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=block,
+                                                return_lse=True)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(lse, lse_ref)           # the LSE stays in packed row order
+
+
+def test_scatter_store_reports_out_of_range_rows():
+    tokens, heads = 256, 1
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn((1, tokens, heads, 128), generator=g).to(torch.bfloat16).to(DEV)
+               for _ in range(3))
+    route = torch.ones((heads, 2, 2), dtype=torch.bool)
+    counts, indices = kernels.pack_boolean_rows(route.to(DEV))
+    rows = torch.arange(tokens, dtype=torch.int32)
+    rows[7] = tokens + 5                       # no row is written to token 7
+    out = torch.zeros_like(q)
+    kernels.block_sparse_attention(q, k, v, counts, indices, out=out, out_rows=rows.to(DEV))
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="out of range"):
+        _native.check_device_errors()
+    assert out[0, 7].abs().sum().item() == 0
+    assert out[0, 8].abs().sum().item() > 0
