@@ -1,9 +1,10 @@
 """Freeze golden fixtures from the reference study itself.
 
-Run in a container where the reference checkout is mounted (it is imported
-from ``$BSA_REFERENCE``, default ``/root/reference``)::
+Run in a container where the reference checkout is mounted; it is imported
+from the directory named by ``$BSA_REFERENCE`` (the script's default is the
+build container's mount point)::
 
-    python tests/golden/make_golden.py
+    BSA_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Inputs are regenerated in the tests from the seeded generators of
 ``dit_sparse_atten_b200.synthetic`` and checked against the SHA-256 digests
