@@ -30,6 +30,7 @@ import sys
 import time
 from datetime import timedelta
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 import torch
@@ -55,6 +56,8 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-route-stage", action="store_true")
+    p.add_argument("--no-gpu-comparator", action="store_true",
+                   help="skip timing the reference's own GPU path (compiled FlexAttention)")
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="target CPU time of the cpu_baseline sample")
     return p.parse_args(argv)
@@ -197,15 +200,108 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------
-# CPU baseline: the reference's algorithm on the host (oracle port)
+# CPU baseline: the reference's own CPU code (baseline/_ref), else the oracle port
 # ----------------------------------------------------------------------------
 
-class CpuSample:
-    """Per-(branch, head) query-block work of the config-4 layer on the host.
+def reference_root():
+    """Directory that holds the reference's ``attention_backends`` package:
+    ``$BSA_REFERENCE`` if set, else ``baseline/_ref`` (the reference installed
+    unmodified with pip), else None."""
+    candidates = []
+    if os.environ.get("BSA_REFERENCE"):
+        candidates.append(Path(os.environ["BSA_REFERENCE"]))
+    candidates.append(REPO / "baseline" / "_ref")
+    for root in candidates:
+        if (root / "attention_backends" / "flex.py").exists():
+            return root
+    return None
 
-    The reference's CPU path (sparse.py:670-751 semantics): gather the kept key
-    blocks of one (head, query block), masked softmax, PV, in float32.
-    """
+
+def load_reference():
+    """``(modules, None)`` with the reference's flex / sparse / spatial /
+    layout_ops modules, or ``(None, reason)`` when it is not installed."""
+    root = reference_root()
+    if root is None:
+        return None, "reference package not installed (no baseline/_ref, no $BSA_REFERENCE)"
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    try:
+        from attention_backends import flex, layout_ops, sparse, spatial
+    except Exception as exc:  # a broken install is reported, not fatal
+        return None, f"reference import failed: {exc!r}"
+    return SimpleNamespace(flex=flex, sparse=sparse, spatial=spatial, layout_ops=layout_ops,
+                           root=str(root)), None
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_threads():
+    return os.cpu_count() or 1
+
+
+def reference_routes(ref, cfg, heads):
+    """Config-4 routes of the first ``heads`` heads per branch, made by the
+    reference's own rule: ``_top_mass_route`` on the blob scores, then the
+    first-frame sink (``flex.py:83-94,550-566``)."""
+    scores = blob_scores(cfg)
+    routes = []
+    for b in range(cfg.batch):
+        r = ref.flex._top_mass_route(scores[b, :heads], cfg.mass_target, cfg.keep)
+        r[..., :cfg.sink_blocks] = True
+        routes.append(r)
+    return routes
+
+
+class RefCpuAttention:
+    """The reference's CPU sparse attention, ``sparse_chunk(use_triton=False)``
+    (``sparse.py:670-751``), on (branch, query-block) rows of config 4 over a
+    subset of heads (its route statistics included, as the reference computes
+    them).  Each call takes the next query blocks, branches alternating."""
+
+    kind = "reference"
+
+    def __init__(self, ref, cfg, heads=8):
+        self.ref, self.cfg, self.heads = ref, cfg, heads
+        self.routes = reference_routes(ref, cfg, heads)
+        g = torch.Generator().manual_seed(41)
+        shape = (1, cfg.tokens, heads, cfg.head_dim)
+        self.qkv = [torch.randn(shape, generator=g).to(torch.bfloat16).float() for _ in range(3)]
+        self.stats = ref.sparse._empty_route_stats(heads, cfg.blocks, "cpu")
+        self.cursor = 0
+
+    def describe(self, rows, seconds):
+        return (f"{rows} (branch, query-block) rows x {self.heads} heads of config 4 through the "
+                f"reference's sparse_chunk(use_triton=False), float32 ({seconds:.1f} s)")
+
+    def run(self, rows):
+        cfg, q, k, v = self.cfg, *self.qkv
+        flops = 0.0
+        for _ in range(rows):
+            idx = self.cursor % (cfg.batch * cfg.blocks)
+            self.cursor += 1
+            b, qb = idx % cfg.batch, (idx // cfg.batch * 37) % cfg.blocks
+            route = self.routes[b]
+            self.ref.sparse.sparse_chunk(q, k, v, route, cfg.block, qb * cfg.block,
+                                         (qb + 1) * cfg.block, cfg.head_dim ** -0.5, self.stats,
+                                         use_triton=False)
+            flops += 4.0 * cfg.block ** 2 * cfg.head_dim * float(route[:, qb].sum())
+        return flops
+
+
+class PortCpuAttention:
+    """Fallback when the reference is not installed: the oracle port of the
+    same CPU path (gather the kept key blocks of one (head, query block),
+    masked softmax, PV, float32)."""
+
+    kind = "port"
 
     def __init__(self, cfg):
         from oracle import route as oroute
@@ -219,13 +315,16 @@ class CpuSample:
                     for _ in range(3)]
         self.cursor = 0
 
-    def run(self, qblocks):
-        """Attention for the next ``qblocks`` query blocks; returns kept FLOPs."""
+    def describe(self, rows, seconds):
+        return (f"{rows} (branch, head, query-block) rows of config 4 through the numpy "
+                f"oracle port (float32, {seconds:.1f} s)")
+
+    def run(self, rows):
         from oracle import attention as oatt
         cfg = self.cfg
         q, k, v = self.qkv
         flops = 0.0
-        for _ in range(qblocks):
+        for _ in range(rows):
             idx = self.cursor % (cfg.batch * cfg.heads * cfg.blocks)
             self.cursor += 1
             b, rest = divmod(idx, cfg.heads * cfg.blocks)
@@ -237,32 +336,68 @@ class CpuSample:
         return flops
 
 
-def cpu_threads():
-    return os.cpu_count() or 1
+def cpu_attention_sample(cfg):
+    ref, _why = load_reference()
+    return RefCpuAttention(ref, cfg) if ref is not None else PortCpuAttention(cfg)
+
+
+def reference_cpu_stages(ref, cfg, heads=4):
+    """The reference's route decision and spatial reorder on the host, on
+    ``heads`` of the 40 heads, scaled to one config-4 layer (2 branches x 40
+    heads): sampled mass S = 16 -> persistence prior -> ``_top_mass_route`` ->
+    sink -> ``pack_boolean_rows`` (``flex.py:205-251,535-541,83-94``,
+    ``layout_ops.py:128-151``), and ``reorder_qkv`` + ``restore``
+    (``spatial.py:86-93``, CPU ``index_select``)."""
+    scale_to_layer = cfg.batch * cfg.heads / heads
+    g = torch.Generator().manual_seed(5)
+    shape = (1, cfg.tokens, heads, cfg.head_dim)
+    q, k, v = (torch.randn(shape, generator=g).to(torch.bfloat16) for _ in range(3))
+    prev = reference_routes(ref, cfg, heads)[1]
+    t0 = time.perf_counter()
+    mass = ref.flex._sampled_block_mass(q, k, cfg.block, samples=16)
+    t1 = time.perf_counter()
+    mass = mass + 0.5 * mass.mean(-1, keepdim=True) * prev.float()
+    route = ref.flex._top_mass_route(mass, cfg.mass_target, cfg.keep)
+    route[..., :cfg.sink_blocks] = True
+    ref.layout_ops.pack_boolean_rows(route)
+    t2 = time.perf_counter()
+    layout = ref.spatial.build_spatial_layout(cfg.grid, cfg.block)
+    t3 = time.perf_counter()
+    qp, kp, vp = layout.reorder_qkv(q, k, v)
+    layout.restore(vp)
+    t4 = time.perf_counter()
+    return {"route_mass_s_per_layer": (t1 - t0) * scale_to_layer,
+            "route_select_pack_s_per_layer": (t2 - t1) * scale_to_layer,
+            "reorder_restore_s_per_layer": (t4 - t3) * scale_to_layer,
+            "spatial_layout_build_s": t3 - t2,
+            "sample": f"{heads} of {cfg.heads} heads of one branch, scaled x{scale_to_layer:g} "
+                      "to a config-4 layer (2 branches x 40 heads)"}
 
 
 def run_cpu_baseline(cfg, seconds):
     torch.set_num_threads(cpu_threads())
-    sample = CpuSample(cfg)
-    sample.run(2)  # warm-up
-    flops, t0, blocks = 0.0, time.perf_counter(), 0
-    while time.perf_counter() - t0 < seconds or blocks < 8:
-        flops += sample.run(4)
-        blocks += 4
+    sample = cpu_attention_sample(cfg)
+    sample.run(1)  # warm-up
+    flops, t0, rows = 0.0, time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds or rows < 4:
+        flops += sample.run(2)
+        rows += 2
     dt = time.perf_counter() - t0
-    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-            "sample": f"{blocks} (branch, head, query-block) rows of config 4 through the numpy "
-                      f"oracle port (float32, {dt:.1f} s)"}
+    line = {"value": flops / dt / 1e12, "unit": UNIT, "cores": cpu_threads(), "kind": sample.kind,
+            "cpu_model": cpu_model(), "sample": sample.describe(rows, dt)}
+    if sample.kind == "reference":
+        line["stages"] = reference_cpu_stages(sample.ref, cfg)
+    return line
 
 
 def run_reference_arm(args):
-    """``--impl reference``: the reference's CPU algorithm, rank 0 only."""
+    """``--impl reference``: the reference's CPU implementation, rank 0 only."""
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     cfg = layer_config(40)
     torch.set_num_threads(cpu_threads())
-    sample = CpuSample(cfg)
-    per_step = 6
+    sample = cpu_attention_sample(cfg)
+    per_step = 1
     for _ in range(max(1, args.warmup)):
         sample.run(per_step)
     flops, t0 = 0.0, time.perf_counter()
@@ -277,10 +412,10 @@ def run_reference_arm(args):
         "data": "synthetic (seeded N(0,1) bf16-valued Q/K/V; blob routes of config 4)",
         "config": {"workload": "config4_wan14b_720p: 57,600 tokens, CFG batch 2, 40 heads, "
                                "head_dim 128, keep cap 0.625, sink 29",
-                   "step_sample": f"{per_step} (branch, head, query-block) rows per step"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{per_step * args.steps} query-block rows of config 4 "
-                                   "(oracle port of the reference sparse path)"},
+                   "step_sample": sample.describe(per_step, dt / args.steps)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(),
+                         "kind": sample.kind, "cpu_model": cpu_model(),
+                         "sample": sample.describe(per_step * args.steps, dt)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -422,6 +557,7 @@ def main(argv=None):
 
     # per-stage breakdown (one extra step, rank-local)
     stages = {}
+    comparator = None
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     qh, kh, vh = (q, k, v) if P == 1 else (None, None, None)
     if P == 1:
@@ -447,6 +583,13 @@ def main(argv=None):
                                       layout.neighbors(device)))
             stages.update(bootstrap_stage(cfg, qp, kp, vp, kernels, stream))
             stages.update(prologue_stage(cfg, layout, kernels, device, stream))
+        if not args.no_gpu_comparator:
+            try:
+                comparator = gpu_comparator(cfg, q, k, v, qp, kp, vp, local_route, counts,
+                                            indices, stages, kernels)
+            except Exception as exc:   # the reference's own code failed: report, go on
+                comparator = {"unavailable": f"reference GPU path raised {exc!r}"[:400]}
+            torch.cuda.synchronize()
 
     peaks, peak_src = load_peaks()
     local_flops = kept_flops(local_route, cfg.tokens, cfg.block, cfg.head_dim)
@@ -481,6 +624,7 @@ def main(argv=None):
                                if pipe is not None else ")")),
             "l2": "inputs (3 x 1.18 GB) exceed L2; no flush"},
         "stages": stages,
+        **({"gpu_comparator": comparator} if comparator is not None else {}),
         "roofline": roofline,
         # pack + attention per step (the unpack is folded into the attention's
         # store); the chunked exchange runs gather, attention and unpack per chunk
@@ -559,6 +703,113 @@ def bootstrap_stage(cfg, qp, kp, vp, kernels, stream):
     B, T, H, D = qp.shape
     return {"bootstrap_dense_and_mass_ms": ms,
             "bootstrap_dense_tflops": 4.0 * B * H * T * T * D / ms / 1e9}
+
+
+def gpu_comparator(cfg, q, k, v, qp, kp, vp, route_all, counts, indices, stages, kernels,
+                   reps=5):
+    """The reference's own GPU path on this GPU, on the same config-4 inputs and
+    routes, stage by stage as its stage profiler does (``profiles/flex_route.py:53-127``):
+    compiled FlexAttention over ``_build_block_mask`` of the same boolean route,
+    ``_sampled_block_mass`` (S = 16), prior + ``_top_mass_route`` + sink +
+    ``_build_block_mask``, the Triton ``reorder_qkv`` and ``restore``, the
+    exact bootstrap (dense FlexAttention with LSE + ``_block_attention_mass``)
+    and dense SDPA.  Each CFG branch is one batch-1 call, as the reference
+    runs them.  Times are CUDA-event medians; this repo's figures for the same
+    stages come from ``stages`` and the ratios are reference ms / this ms."""
+    ref, why = load_reference()
+    if ref is None:
+        return {"unavailable": why}
+    import torch.nn.functional as F
+
+    B, T, H, D = qp.shape
+    scale = D ** -0.5
+    block = cfg.block
+
+    def timed(fn, n=reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(n):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    res = {"reference": f"{ref.root}: the reference's attention_backends, unmodified "
+                        f"(torch {torch.__version__}, FlexAttention compiled by Inductor)"}
+    t0 = time.perf_counter()
+    masks = [ref.flex._build_block_mask(route_all[b], T, block) for b in range(B)]
+
+    def flex_sparse():
+        return [ref.flex._flex_output(qp[b:b + 1], kp[b:b + 1], vp[b:b + 1], masks[b], block,
+                                      True, scale=scale) for b in range(B)]
+
+    theirs = flex_sparse()
+    torch.cuda.synchronize()
+    res["compile_s"] = time.perf_counter() - t0
+    # same inputs, same routes: the reference's output against this repo's kernel
+    mine = kernels.block_sparse_attention(qp, kp, vp, counts, indices, block=block)
+    diff = torch.cat([(theirs[b][0].float() - mine[b].float()).abs().flatten()
+                      for b in range(B)])
+    res["flex_vs_bsa_max_abs"] = float(diff.max())
+    res["flex_vs_bsa_mean_abs"] = float(diff.mean())
+    del theirs, mine, diff
+    res["flex_sparse_ms"] = timed(flex_sparse)
+
+    def sampled():
+        return [ref.flex._sampled_block_mass(qp[b:b + 1], kp[b:b + 1], block, samples=16,
+                                             scale=scale) for b in range(B)]
+
+    masses = sampled()
+    res["sampled_mass_ms"] = timed(sampled)
+
+    def select_and_mask():
+        for b in range(B):
+            m = masses[b] + 0.5 * masses[b].mean(-1, keepdim=True) * route_all[b].float()
+            r = ref.flex._top_mass_route(m, cfg.mass_target, cfg.keep)
+            r[..., :cfg.sink_blocks] = True
+            ref.flex._build_block_mask(r, T, block)
+
+    res["select_and_mask_ms"] = timed(select_and_mask)
+    del masses, masks
+
+    layout = ref.spatial.build_spatial_layout(cfg.grid, block)
+    res["reorder_ms"] = timed(lambda: layout.reorder_qkv(q, k, v))
+    res["restore_ms"] = timed(lambda: layout.restore(q))
+
+    res["sdpa_dense_ms"] = timed(lambda: F.scaled_dot_product_attention(
+        q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=scale), n=3)
+
+    dense_flex = ref.flex._flex_kernel(True)
+
+    def exact_bootstrap():
+        for b in range(B):
+            qb, kb, vb = qp[b:b + 1], kp[b:b + 1], vp[b:b + 1]
+            _o, lse = dense_flex(qb.transpose(1, 2), kb.transpose(1, 2), vb.transpose(1, 2),
+                                 scale=scale, return_lse=True)
+            ref.flex._block_attention_mass(qb, kb, lse, block, scale=scale)
+
+    res["exact_bootstrap_ms"] = timed(exact_bootstrap, n=3)
+    res["total_s"] = time.perf_counter() - t0
+
+    pairs = {"attention": ("flex_sparse_ms", "attention_ms"),
+             "sampled_mass": ("sampled_mass_ms", "route_mass_ms"),
+             "select": ("select_and_mask_ms", "route_select_ms"),
+             "reorder": ("reorder_ms", "pack_ms"),
+             "exact_bootstrap": ("exact_bootstrap_ms", "bootstrap_dense_and_mass_ms")}
+    res["speedup"] = {name: res[a] / stages[b] for name, (a, b) in pairs.items()
+                      if stages.get(b)}
+    if stages.get("attention_ms") and stages.get("pack_ms"):
+        # the layer as the reference runs it (pack, sparse attention, restore)
+        # against this repo's step (pack, attention with the unpack in its store)
+        theirs_layer = res["reorder_ms"] + res["flex_sparse_ms"] + res["restore_ms"]
+        res["layer_ms"] = theirs_layer
+        res["speedup"]["layer"] = theirs_layer / (stages["pack_ms"] + stages["attention_ms"])
+    return res
 
 
 def prologue_stage(cfg, layout, kernels, device, stream):

@@ -45,7 +45,6 @@ SIGNATURES = {
                                   _I32),
     "bsa_attention_dense_block_mass": ([_P, _P, _P, _I64, _I64, _I64, _I32, _I64, _I64, _I64,
                                         _F32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], _I32),
-    "bsa_exp2": ([_P, _P, _I64, _I32, _P], _I32),
 }
 
 DEVICE_ERRORS = {

@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -34,13 +35,16 @@ int ok() {
 }
 
 int sm_count() {
-  static int cached[64] = {};
+  static std::atomic<int> cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 148;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cached[dev] = n;
+  if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -452,6 +456,18 @@ int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(BSA_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  // The kernels run on the caller's stream with the current device's scratch:
+  // a stream of another device is refused rather than launched with the
+  // wrong device's address.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int stream_dev = dev;
+  e = cudaStreamGetDevice(st, &stream_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_noalloc: cudaStreamGetDevice");
+  if (stream_dev != dev)
+    return fail(BSA_ERR_INVALID_ARGUMENT,
+                "the stream belongs to device %d but device %d is current", stream_dev, dev);
+  // The address is cached for the life of the process; it does not survive
+  // cudaDeviceReset of this device.
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(scratch_mu);
@@ -468,7 +484,6 @@ int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_
   const int64_t tail = tokens - (q_blocks - 1) * block;
   const float bias_full = logf(static_cast<float>(block) / static_cast<float>(samples));
   const float bias_tail = logf(static_cast<float>(tail) / static_cast<float>(samples));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(scratch);
   for (int64_t b = 0; b < batch; ++b) {
     for (int64_t h0 = 0; h0 < heads; h0 += hc_max) {
@@ -486,6 +501,7 @@ int bsa_sampled_mass_noalloc(const void* q, const void* k, int64_t batch, int64_
       rc = encode_bhtd(&tk, base + region, 1, n_rows, hc, head_dim, n_rows * hc * head_dim,
                        hc * head_dim, head_dim, 128, &tm);
       if (rc != BSA_OK) return rc;
+      if (tm) return fail(BSA_ERR_UNSUPPORTED, "sampled rows must be row-major [rows, heads, D]");
       bsa::MassArgs a{};
       a.batch = 1;
       a.heads = hc;
@@ -662,15 +678,6 @@ int bsa_attention_dense_block_mass(const void* q, const void* k, const void* v, 
                                          static_cast<int32_t>(blocks), mass,
                                          static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "bsa_attention_dense_block_mass mass launch");
-  return ok();
-}
-
-int bsa_exp2(const float* x, float* y, int64_t n, int32_t mode, void* stream) {
-  if (x == nullptr || y == nullptr) return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
-  if (mode != 0 && mode != 1) return fail(BSA_ERR_INVALID_ARGUMENT, "mode must be 0 or 1");
-  if (n < 0) return fail(BSA_ERR_INVALID_ARGUMENT, "negative size");
-  cudaError_t e = bsa::launch_exp2(x, y, n, mode, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "bsa_exp2 launch");
   return ok();
 }
 

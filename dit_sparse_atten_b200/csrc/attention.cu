@@ -40,6 +40,8 @@
 // Every mbarrier wait is bounded (bsa::mbar_wait); on a timeout the CTA sets
 // kErrWaitTimeout in the caller's error word, drains its in-flight copies and
 // MMAs, frees TMEM and exits.
+#include <atomic>
+
 #include "bsa_kernels.h"
 
 namespace bsa {
@@ -566,11 +568,11 @@ cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
   using L = AttnLayout<BK>;
   // The layout needs kUsed bytes from a 1024-byte-aligned base; ask for up to
   // 1 KB of slack within the opt-in limit (the kernel checks and reports).
-  static int smem_bytes[64] = {};
+  static std::atomic<int> smem_bytes[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  int bytes = (dev >= 0 && dev < 64) ? smem_bytes[dev] : 0;
+  int bytes = (dev >= 0 && dev < 64) ? smem_bytes[dev].load(std::memory_order_acquire) : 0;
   if (bytes == 0) {
     int optin = 0;
     e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -580,7 +582,7 @@ cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
     e = cudaFuncSetAttribute(bsa_attention_kernel<BK, kDenseMass>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) smem_bytes[dev] = bytes;
+    if (dev >= 0 && dev < 64) smem_bytes[dev].store(bytes, std::memory_order_release);
   }
   const dim3 grid(static_cast<unsigned>(a.q_blocks), static_cast<unsigned>(a.heads),
                   static_cast<unsigned>(a.batch));

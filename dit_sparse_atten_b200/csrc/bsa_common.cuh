@@ -88,11 +88,13 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity.  Returns false when the
-// CTA is aborting (flag set by any thread) or the wait timed out, in which
+// Bounded wait for the phase with the given parity, giving up after
+// ``timeout_ns`` of %globaltimer (or kWaitMaxPolls polls).  Returns false when
+// the CTA is aborting (flag set by any thread) or the wait timed out, in which
 // case the abort flag and the caller's error word are set.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err_word) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag, int* err_word,
+                                              uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t poll = 1; poll < kWaitMaxPolls; ++poll) {
@@ -104,12 +106,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         *abort_flag = 1;
         return false;
       }
-      if (global_timer_ns() - start > kWaitTimeoutNs) break;
+      if (global_timer_ns() - start > timeout_ns) break;
     }
   }
   *abort_flag = 1;
   if (err_word) atomicOr(err_word, kErrWaitTimeout);
   return false;
+}
+
+// The kernels' wait: mbar_wait_for with the library-wide limit kWaitTimeoutNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int* err_word) {
+  return mbar_wait_for(bar, parity, abort_flag, err_word, kWaitTimeoutNs);
 }
 
 // True when an earlier timeout was recorded in the error word: kernels then

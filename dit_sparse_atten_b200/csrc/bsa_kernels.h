@@ -164,7 +164,4 @@ cudaError_t launch_block_mass(const float* block_lse, const float* lse, int64_t 
                               int64_t tokens, int64_t heads, int32_t blocks, float* mass,
                               cudaStream_t stream);
 
-// ---- diagnostics ------------------------------------------------------------
-cudaError_t launch_exp2(const float* x, float* y, int64_t n, int mode, cudaStream_t stream);
-
 }  // namespace bsa

@@ -12,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 CSRC = Path(__file__).resolve().parent
@@ -50,14 +51,21 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> Path:
     nvcc = nvcc_path()
     objdir = REPO / "_build"
     objdir.mkdir(exist_ok=True)
-    objects = []
+    objects, commands = [], []
     for src in SOURCES:
         obj = objdir / (src.stem + ".o")
-        cmd = [nvcc, *NVCC_FLAGS, "-dc" if False else "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
         if verbose_ptxas:
             cmd[1:1] = ["-Xptxas", "-v"]
-        subprocess.run(cmd, check=True)
+        commands.append(cmd)
         objects.append(str(obj))
+    # one nvcc per translation unit, in parallel
+    with ThreadPoolExecutor(max_workers=min(len(commands), os.cpu_count() or 1)) as pool:
+        for done in pool.map(lambda c: subprocess.run(c, capture_output=True, text=True),
+                             commands):
+            sys.stdout.write(done.stdout)
+            sys.stderr.write(done.stderr)
+            done.check_returncode()
     tmp = LIBRARY.with_suffix(".so.tmp")
     subprocess.run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a",
                     "-o", str(tmp), *objects], check=True)

@@ -18,6 +18,8 @@
 // One CTA per (128 query rows, head, batch).  The 128-key tiles stream through
 // a TMA ring: pass 1 computes every row's log-sum-exp, pass 2 the normalised
 // per-block sums.
+#include <atomic>
+
 #include "bsa_kernels.h"
 
 namespace bsa {
@@ -598,15 +600,17 @@ __global__ void __launch_bounds__(256) sampled_mass_reduce_kernel(const MassArgs
 template <int LOG2S, bool kRound>
 cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                             cudaStream_t stream) {
-  static bool configured[64] = {};
+  // Per-device flag; concurrent callers may both set the attribute, which is
+  // harmless, but the flag itself must not be a data race.
+  static std::atomic<bool> configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     e = cudaFuncSetAttribute(sampled_mass_kernel2<LOG2S, kRound>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kMass2Smem);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
   const dim3 grid(static_cast<unsigned>((a.n_rows + kTile - 1) / kTile),
                   static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));

@@ -510,16 +510,3 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  _native.ptr(lse), _native.err_word(device).data_ptr(), _stream(device))
     return (out, lse) if return_lse else out
 
-
-# ----------------------------------------------------------------------------
-# diagnostics
-# ----------------------------------------------------------------------------
-
-def exp2(x: torch.Tensor, mode: str = "poly") -> torch.Tensor:
-    """2^x through the softmax kernels' MUFU (``mode="mufu"``) or polynomial path."""
-    device = _require_cuda(x)
-    x = x.to(torch.float32).contiguous()
-    y = torch.empty_like(x)
-    _native.call("bsa_exp2", x.data_ptr(), y.data_ptr(), x.numel(), 1 if mode == "poly" else 0,
-                 _stream(device))
-    return y

@@ -227,7 +227,9 @@ BSA_API int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_
  * Calls on one device share the scratch: two calls must not be in flight at
  * the same time (on different streams or threads) or they race.  The first
  * call on a device looks up the scratch address (cudaGetSymbolAddress) and
- * configures the kernels, so make it before any stream capture.
+ * configures the kernels, so make it before any stream capture; the address
+ * is cached for the process and does not survive cudaDeviceReset.  The
+ * stream must belong to the current device (else BSA_ERR_INVALID_ARGUMENT).
  * Same limits as bsa_sampled_mass (samples in {1,...,32}, head_dim == 128,
  * q_blocks <= 4096) and block in {32, 64, 128}.
  */
@@ -324,8 +326,6 @@ BSA_API int bsa_attention_dense_block_mass(const void* q, const void* k, const v
                                            void* out, int64_t out_stride_b, int64_t out_stride_t,
                                            int64_t out_stride_h, float* lse, float* block_lse,
                                            float* mass, int32_t* err_word, void* stream);
-
-BSA_API int bsa_exp2(const float* x, float* y, int64_t n, int32_t mode, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,8 +1,7 @@
 """Freeze golden fixtures from the reference study itself.
 
 Run in a container where the reference checkout is mounted; it is imported
-from the directory named by ``$BSA_REFERENCE`` (the script's default is the
-build container's mount point)::
+from the directory named by ``$BSA_REFERENCE``, which must be set::
 
     BSA_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
@@ -54,7 +53,10 @@ import torch
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
 sys.path.insert(0, str(REPO))
-sys.path.insert(0, os.environ.get("BSA_REFERENCE", "/root/reference"))
+if not os.environ.get("BSA_REFERENCE"):
+    raise SystemExit("set BSA_REFERENCE to the reference checkout (the directory that holds "
+                     "attention_backends/)")
+sys.path.insert(0, os.environ["BSA_REFERENCE"])
 
 from attention_backends import flex as ref_flex  # noqa: E402
 from attention_backends import layout_ops as ref_layout_ops  # noqa: E402

@@ -184,19 +184,22 @@ def test_config4_720p_layer_morton(golden):
 
 
 def test_exp2_paths_accuracy():
-    """Both softmax exponentials against float64 and CUDA's exp2f (torch.exp2)."""
+    """Both softmax exponentials against float64 and CUDA's exp2f (torch.exp2),
+    evaluated by the test-only diagnostic library."""
+    import diag
+
     x = torch.cat([torch.linspace(-126.0, 8.0, 1 << 20), torch.tensor([0.0, -0.5, 0.5, 7.99])])
     ref = np.exp2(x.double().numpy())
     xd = x.to(DEV)
-    poly = kernels.exp2(xd, "poly").double().cpu().numpy()
-    mufu = kernels.exp2(xd, "mufu").double().cpu().numpy()
+    poly = diag.exp2(xd, "poly").double().cpu().numpy()
+    mufu = diag.exp2(xd, "mufu").double().cpu().numpy()
     cuda_exp2f = torch.exp2(xd).double().cpu().numpy()
     normal = x.numpy() >= -125.0            # results >= 2^-125 stay normal floats
     assert (np.abs(poly - ref) / ref)[normal].max() <= 1e-4
     assert np.abs(poly - ref)[~normal].max() <= 2.0 ** -125 * 1e-3
     assert (np.abs(mufu - ref) / ref)[normal].max() <= 2.0 ** -21
     assert (np.abs(poly - cuda_exp2f) / cuda_exp2f)[normal].max() <= 1e-4 + 2.0 ** -22
-    below = kernels.exp2(torch.tensor([-200.0, -1000.0], device=DEV), "poly").cpu()
+    below = diag.exp2(torch.tensor([-200.0, -1000.0], device=DEV), "poly").cpu()
     assert (below >= 0).all() and (below < 2.0 ** -125).all()
 
 

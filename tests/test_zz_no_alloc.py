@@ -54,6 +54,35 @@ def test_matches_workspace_path_twice(B, T, H, block, samples):
         torch.testing.assert_close(got, ref, atol=ATOL, rtol=RTOL)
 
 
+def test_allocates_nothing_and_rewrites_its_scratch():
+    """After a warm-up call, a call changes neither torch's allocated bytes nor
+    the device's free memory; a large case followed by a smaller one with other
+    inputs still matches the workspace path, so every call writes all of the
+    scratch it reads (nothing is left over from the call before)."""
+    big_q, big_k = inputs(1, 57600, 12, seed=11)
+    small_q, small_k = inputs(2, 3000, 5, seed=12)
+    small_ref = kernels.sampled_block_mass(small_q, small_k, 128, 16, one_pass=False)
+    big_mass = torch.empty((1, 12, 450, 450), dtype=torch.float32, device=DEV)
+    small_mass = torch.empty_like(small_ref)
+
+    def call(q, k, out):
+        _native.call("bsa_sampled_mass_noalloc", q.data_ptr(), k.data_ptr(), q.shape[0],
+                     q.shape[1], q.shape[2], 128, 128, 16, 128 ** -0.5, 1, out.data_ptr(),
+                     _native.err_word(q.device).data_ptr(),
+                     torch.cuda.current_stream(q.device).cuda_stream)
+
+    call(big_q, big_k, big_mass)               # warm-up: set-up happens here
+    torch.cuda.synchronize()
+    allocated, free = torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0]
+    call(big_q, big_k, big_mass)
+    call(small_q, small_k, small_mass)
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    assert torch.cuda.memory_allocated() == allocated
+    assert torch.cuda.mem_get_info()[0] == free
+    torch.testing.assert_close(small_mass, small_ref, atol=ATOL, rtol=RTOL)
+
+
 def test_rejects_sizes_beyond_the_scratch():
     # 2049 blocks x 32 samples = 65,568 sampled rows: 2 * 65,568 * 256 bytes for
     # one head already exceeds the 32 MiB scratch.  The call must fail before
