@@ -18,7 +18,8 @@ path needs CUDA bf16 tensors with head_dim 128 and raises otherwise.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, fields
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -173,62 +174,208 @@ def _fp32_mean_of_count(count, numel):
     return float(np.float32(np.float32(count) / np.float32(numel)))
 
 
+# ----------------------------------------------------------------------------
+# Backend state: one RouteState per (layer, branch, shape, device, layout) key,
+# and a PhaseLog of what the backend did.
+# ----------------------------------------------------------------------------
+
+PHASES = ("dense_bootstrap", "sampled_bootstrap", "exact_refresh", "sampled_update",
+          "sparse_reuse", "dense_dispatch", "first_layer_dense")
+
+
+class RouteResult(NamedTuple):
+    """A freshly chosen route: bool route, its frontier (or None), per-plane
+    kept counts (int64, or None) and the CSR the attention kernel reads."""
+    route: torch.Tensor
+    frontier: torch.Tensor | None
+    kept: torch.Tensor | None
+    block_mask: "BlockRoute"
+
+
+class PendingRoute(NamedTuple):
+    """A route computed on the side stream, adopted at the next call."""
+    result: RouteResult
+    source_step: int
+    ready: torch.cuda.Event
+
+
+@dataclass
+class RouteState:
+    """Reusable route of one layer and CFG branch.
+
+    Item access (``state["route"]``, ``state.get("dense")``, ``"pending" in
+    state``) is kept because the reference exposes its per-route state as
+    plain dicts that callers and tests read and inject (``backend.state``).
+    """
+    route: torch.Tensor | None = None
+    frontier: torch.Tensor | None = None
+    block_mask: object = None
+    kept: torch.Tensor | None = None
+    step: int = 0
+    layout: object = None
+    grid: tuple | None = None
+    keep: float | None = None
+    frontier_fraction: float | None = None
+    dense: bool = False
+    pending: PendingRoute | None = None
+
+    @classmethod
+    def coerce(cls, value):
+        if isinstance(value, cls):
+            return value
+        names = {f.name for f in fields(cls)}
+        return cls(**{k: v for k, v in dict(value).items() if k in names})
+
+    def adopt(self, result: RouteResult, step: int | None = None):
+        self.route, self.frontier, self.kept, self.block_mask = result
+        if step is not None:
+            self.step = step
+
+    def drop_route(self):
+        self.route = self.frontier = self.kept = self.block_mask = None
+
+    # mapping view ---------------------------------------------------------
+    def __contains__(self, name):
+        return name in _STATE_FIELDS and not (name == "pending" and self.pending is None)
+
+    def __getitem__(self, name):
+        if name not in self:
+            raise KeyError(name)
+        return getattr(self, name)
+
+    def __setitem__(self, name, value):
+        if name not in _STATE_FIELDS:
+            raise KeyError(name)
+        setattr(self, name, value)
+
+    def get(self, name, default=None):
+        return getattr(self, name) if name in self else default
+
+
+_STATE_FIELDS = frozenset(f.name for f in fields(RouteState))
+
+
+class ReleasedRoute(NamedTuple):
+    keep: float | None
+    frontier_fraction: float | None
+    dense: bool
+
+
+class PhaseLog:
+    """How often each phase ran, and the keep statistics of released routes."""
+
+    def __init__(self):
+        self.counts = dict.fromkeys(PHASES, 0)
+        self.released: list[ReleasedRoute] = []
+
+    def hit(self, phase: str):
+        self.counts[phase] += 1
+
+    def release(self, state: RouteState):
+        self.released.append(ReleasedRoute(state.keep, state.frontier_fraction, bool(state.dense)))
+
+    def summary(self, live) -> dict:
+        """The reference's ``profile_summary`` fields (written by its
+        ``infer.py:_write_timing``) over live and released routes."""
+        live = list(live)
+        routed = [s for s in live if s.route is not None]
+
+        def mean(values):
+            values = [x for x in values if x is not None]
+            return sum(values) / len(values) if values else None
+
+        return {
+            "phase_counts": dict(self.counts),
+            "active_routes": len(routed),
+            "released_routes": len(self.released),
+            "mean_route_keep": mean([s.keep for s in routed] + [r.keep for r in self.released]),
+            "mean_frontier_fraction": mean([s.frontier_fraction for s in routed]
+                                           + [r.frontier_fraction for r in self.released]),
+            "dense_dispatched_routes": sum(bool(s.dense) for s in live)
+            + sum(r.dense for r in self.released),
+        }
+
+
+class _StateTable(dict):
+    """``backend.state``: RouteState values; plain dicts stored by a caller are
+    converted on the way in."""
+
+    def __setitem__(self, key, value):
+        super().__setitem__(key, RouteState.coerce(value))
+
+    def update(self, *args, **kw):
+        for key, value in dict(*args, **kw).items():
+            self[key] = value
+
+    def setdefault(self, key, default=None):
+        if key not in self:
+            self[key] = default if default is not None else RouteState()
+        return self[key]
+
+
+def _validate(c: "FlexReuseConfig"):
+    """Construction-time checks; messages follow the reference (``flex.py:408-443``)."""
+    checks = (
+        (c.block_size == 128,
+         "The minimal flex_reuse backend currently supports only 128-token blocks"),
+        (c.update_interval >= 0, "update_interval must be zero or a positive integer"),
+        (c.sampled_update_interval >= 0,
+         "sampled_update_interval must be zero or a positive integer"),
+        (not (c.update_interval and c.sampled_update_interval),
+         "exact and sampled route updates are mutually exclusive"),
+        (0 < c.route_samples <= c.block_size, "route_samples must be in [1, block_size]"),
+        (c.route_persistence >= 0, "route_persistence must be non-negative"),
+        (c.bootstrap_mode in ("exact", "sampled"), "bootstrap_mode must be 'exact' or 'sampled'"),
+        (c.dense_route_threshold is None or 0 < c.dense_route_threshold <= 1,
+         "dense_route_threshold must be in (0, 1]"),
+        (0 < c.keep <= 1, "keep must be in (0, 1]"),
+        (0 < c.mass_target <= 1, "mass_target must be in (0, 1]"),
+        (c.spatial_microtile_tokens > 0, "spatial_microtile_tokens must be positive"),
+        (c.direction_min_ratio >= 0, "direction_min_ratio must be non-negative"),
+        (c.direction_candidate_bonus >= 0, "direction_candidate_bonus must be non-negative"),
+        (c.route_budget_scale > 0, "route_budget_scale must be positive"),
+        (0 <= c.route_exploration_fraction <= 1, "route_exploration_fraction must be in [0, 1]"),
+        (not c.directional_update or c.spatial_reorder,
+         "directional_update requires spatial_reorder"),
+    )
+    for ok, message in checks:
+        if not ok:
+            raise ValueError(message)
+
+
 class FlexReuseBackend:
-    """Dense bootstrap followed by reuse with optional exact or sampled refresh."""
+    """Dense bootstrap followed by reuse with optional exact or sampled refresh.
+
+    Each call is classified by ``_plan`` into one action (bootstrap, dense
+    dispatch, exact refresh, inline sampled update, sparse reuse) that
+    ``__call__`` runs; route bookkeeping lives in ``RouteState`` and the
+    phase tally in ``PhaseLog``.  The decisions follow the reference's order
+    (``flex.py:652-850``) so routes are refreshed at the same steps.
+    """
 
     name = "flex_reuse"
 
     def __init__(self, config=None, routing_context=None, process_group=None):
         self.config = config or FlexReuseConfig()
-        c = self.config
-        if c.block_size != 128:
-            raise ValueError("The minimal flex_reuse backend currently supports only 128-token blocks")
-        if c.update_interval < 0:
-            raise ValueError("update_interval must be zero or a positive integer")
-        if c.sampled_update_interval < 0:
-            raise ValueError("sampled_update_interval must be zero or a positive integer")
-        if c.update_interval and c.sampled_update_interval:
-            raise ValueError("exact and sampled route updates are mutually exclusive")
-        if not 0 < c.route_samples <= c.block_size:
-            raise ValueError("route_samples must be in [1, block_size]")
-        if c.route_persistence < 0:
-            raise ValueError("route_persistence must be non-negative")
-        if c.bootstrap_mode not in ("exact", "sampled"):
-            raise ValueError("bootstrap_mode must be 'exact' or 'sampled'")
-        if c.dense_route_threshold is not None and not 0 < c.dense_route_threshold <= 1:
-            raise ValueError("dense_route_threshold must be in (0, 1]")
-        if not 0 < c.keep <= 1:
-            raise ValueError("keep must be in (0, 1]")
-        if not 0 < c.mass_target <= 1:
-            raise ValueError("mass_target must be in (0, 1]")
-        if c.spatial_microtile_tokens <= 0:
-            raise ValueError("spatial_microtile_tokens must be positive")
-        if c.direction_min_ratio < 0:
-            raise ValueError("direction_min_ratio must be non-negative")
-        if c.direction_candidate_bonus < 0:
-            raise ValueError("direction_candidate_bonus must be non-negative")
-        if c.route_budget_scale <= 0:
-            raise ValueError("route_budget_scale must be positive")
-        if not 0 <= c.route_exploration_fraction <= 1:
-            raise ValueError("route_exploration_fraction must be in [0, 1]")
-        if c.directional_update and not c.spatial_reorder:
-            raise ValueError("directional_update requires spatial_reorder")
+        _validate(self.config)
         self._routing_context = routing_context
         self.process_group = process_group
         self.dense = DenseBackend()
-        self.state = {}
+        self.state = _StateTable()
         self.route_streams = {}
         self.spatial_layouts = {}
-        self.phase_counts = {
-            "dense_bootstrap": 0,
-            "sampled_bootstrap": 0,
-            "exact_refresh": 0,
-            "sampled_update": 0,
-            "sparse_reuse": 0,
-            "dense_dispatch": 0,
-            "first_layer_dense": 0,
-        }
-        self.finished_routes = []
+        self.log = PhaseLog()
+
+    @property
+    def phase_counts(self):
+        return self.log.counts
+
+    @property
+    def finished_routes(self):
+        return [r._asdict() for r in self.log.released]
+
+    def profile_summary(self):
+        return self.log.summary(self.state.values())
 
     # ------------------------------------------------------------------ context
     def _context(self):
@@ -236,6 +383,14 @@ class FlexReuseBackend:
             return self._routing_context(include_grid=True)
         # Resolved at call time so tests can monkeypatch this module's name.
         return globals()["routing_context"](include_grid=True)
+
+    def _final_step(self, step):
+        c = self.config
+        return c.release_after_final_step and c.total_steps is not None and step >= c.total_steps - 1
+
+    def _before_last_step(self, step):
+        total = self.config.total_steps
+        return total is None or step < total - 1
 
     # ------------------------------------------------------------------ dispatch
     def _global_keep(self, kept, numel):
@@ -248,52 +403,53 @@ class FlexReuseBackend:
             numel = numel * dist.get_world_size(self.process_group)
         return _fp32_mean_of_count(int(total.item()), numel)
 
-    def _activate_pending_route(self, state):
-        pending = state.pop("pending", None)
+    def _refresh_dispatch(self, state: RouteState):
+        """Recompute the route's keep (and frontier) fraction; at or above
+        ``dense_route_threshold`` the state goes dense for good and drops its
+        route (``flex.py:473-493``)."""
+        if state.route is None:
+            state.keep = None
+        else:
+            kept = state.kept
+            if kept is None:
+                kept = state.route.reshape(state.route.shape[0], -1).sum(-1)
+            state.keep = self._global_keep(kept, state.route.numel())
+        f = state.frontier
+        state.frontier_fraction = (None if f is None
+                                   else _fp32_mean_of_count(int(f.sum().item()), f.numel()))
+        threshold = self.config.dense_route_threshold
+        state.dense = bool(threshold is not None and state.keep is not None
+                           and state.keep >= threshold)
+        if state.dense:
+            state.drop_route()
+
+    def _adopt_pending(self, state: RouteState):
+        pending, state.pending = state.pending, None
         if pending is None:
             return
-        torch.cuda.current_stream(pending["route"].device).wait_event(pending["ready"])
-        state.update({
-            "route": pending["route"],
-            "frontier": pending.get("frontier"),
-            "block_mask": pending["block_mask"],
-            "kept": pending.get("kept"),
-            "step": pending["source_step"],
-        })
-        self._update_dispatch(state)
+        torch.cuda.current_stream(pending.result.route.device).wait_event(pending.ready)
+        state.adopt(pending.result, pending.source_step)
+        self._refresh_dispatch(state)
 
-    def _update_dispatch(self, state):
-        threshold = self.config.dense_route_threshold
-        route = state.get("route")
-        keep = None
-        if route is not None:
-            kept = state.get("kept")
-            if kept is None:
-                kept = route.reshape(route.shape[0], -1).sum(-1)
-            keep = self._global_keep(kept, route.numel())
-        state["keep"] = keep
-        frontier = state.get("frontier")
-        state["frontier_fraction"] = (
-            _fp32_mean_of_count(int(frontier.sum().item()), frontier.numel())
-            if frontier is not None else None)
-        state["dense"] = bool(threshold is not None and keep is not None and keep >= threshold)
-        if state["dense"]:
-            state["route"] = None
-            state["block_mask"] = None
-            state["frontier"] = None
-            state["kept"] = None
+    def _install(self, state: RouteState, result, tokens, step=None):
+        if not isinstance(result, RouteResult):
+            result = self._as_result(result, tokens)
+        state.adopt(result, step)
+        self._refresh_dispatch(state)
 
-    def _is_final_step(self, step):
-        return (self.config.release_after_final_step and self.config.total_steps is not None
-                and step >= self.config.total_steps - 1)
+    def _as_result(self, mapping, tokens):
+        """A RouteResult from a reference-style ``{"route": .., "frontier": ..}``
+        mapping (a route producer substituted by a caller)."""
+        route = mapping["route"]
+        block_mask = mapping.get("block_mask")
+        if block_mask is None:
+            block_mask = _build_block_mask(route, tokens, self.config.block_size)
+        return RouteResult(route, mapping.get("frontier"), mapping.get("kept"), block_mask)
 
-    def _release_route(self, key, state):
-        self.finished_routes.append({
-            "keep": state.get("keep"),
-            "frontier_fraction": state.get("frontier_fraction"),
-            "dense": bool(state.get("dense")),
-        })
-        self.state.pop(key, None)
+    def _release(self, key):
+        state = self.state.pop(key, None)
+        if state is not None:
+            self.log.release(state)
 
     # ------------------------------------------------------------------ routes
     def _sink_blocks(self, state):
@@ -302,15 +458,28 @@ class FlexReuseBackend:
             return 0
         return math.ceil((grid[1] * grid[2]) / self.config.block_size)
 
+    def _csr_result(self, result, tokens, layout):
+        route = result.route.bool()
+        frontier = None
+        if layout is not None:
+            frontier = frontier_mask(route, layout.neighbors(route.device))
+        block_mask = BlockRoute(result.counts.unsqueeze(0), result.indices.unsqueeze(0), tokens,
+                                self.config.block_size)
+        return RouteResult(route, frontier, result.kept, block_mask)
+
+    def _result_from_csr(self, state, result, tokens):
+        return self._csr_result(result, tokens, state.get("layout"))
+
     def _sampled_route(self, state, q, k, softmax_scale):
-        """Sampled mass -> prior -> top-mass -> sink -> CSR in two kernels."""
+        """Sampled mass, then either the directional frontier update or the
+        prior + top-mass selection, with the sink and the CSR in the same
+        kernel (``flex.py:508-548``)."""
         c = self.config
         mass = _sampled_block_mass(q, k, c.block_size, samples=c.route_samples,
                                    scale=softmax_scale, query_block_chunk=c.sample_query_block_chunk)
-        previous = state.get("route")
-        layout = state.get("layout")
+        previous, layout = state.get("route"), state.get("layout")
+        tokens = q.shape[1]
         if c.directional_update and previous is not None and layout is not None:
-            # flex.py:517-534 + the sink of :550-566, in one call
             r = kernels.directional_update(
                 mass, previous, layout.neighbors(mass.device), keep=c.keep,
                 persistence=c.route_persistence, min_ratio=c.direction_min_ratio,
@@ -319,107 +488,75 @@ class FlexReuseBackend:
                 expand_q=c.direction_expand_q, expand_k=c.direction_expand_k,
                 expand_joint=c.direction_expand_joint,
                 previous_frontier=state.get("frontier"), sink_blocks=self._sink_blocks(state))
-            return {
-                "route": r.route,
-                "frontier": r.frontier,
-                "kept": r.kept,
-                "block_mask": BlockRoute(r.counts.unsqueeze(0), r.indices.unsqueeze(0),
-                                         q.shape[1], c.block_size),
-            }
-        result = kernels.route_select(
-            mass, prev=previous if c.route_persistence else None,
-            persistence=c.route_persistence, target=c.mass_target, keep=c.keep,
-            sink_blocks=self._sink_blocks(state))
-        return self._result_from_csr(state, result, q.shape[1])
-
-    def _result_from_csr(self, state, result, tokens):
-        route = result.route.bool()
-        layout = state.get("layout")
-        frontier = frontier_mask(route, layout.neighbors(route.device)) if layout is not None else None
-        return {
-            "route": route,
-            "frontier": frontier,
-            "kept": result.kept,
-            "block_mask": BlockRoute(result.counts.unsqueeze(0), result.indices.unsqueeze(0),
-                                     tokens, self.config.block_size),
-        }
-
-    def _add_first_frame_sink(self, state, result):
-        if not self.config.first_frame_sink:
-            return result
-        grid = state.get("grid")
-        if grid is None:
-            return result
-        route = result["route"].clone()
-        route[..., :math.ceil((grid[1] * grid[2]) / self.config.block_size)] = True
-        result = dict(result)
-        result["route"] = route
-        result.pop("kept", None)
-        result.pop("block_mask", None)
-        layout = state.get("layout")
-        if layout is not None:
-            result["frontier"] = frontier_mask(route, layout.neighbors(route.device))
-        return result
-
-    def _dense_for_exact_route(self, q, k, v, softmax_scale, dense_only):
-        """Dense output plus its exact block mass from one attention pass, or
-        SDPA and no mass (computed later from q, k) for inputs that kernel
-        does not take."""
-        output, mass = _dense_and_mass(q, k, v, self.config.block_size, softmax_scale)
-        if output is None:
-            return self.dense(q, k, v, **dense_only), None
-        return output, mass[0]
+            csr = BlockRoute(r.counts.unsqueeze(0), r.indices.unsqueeze(0), tokens, c.block_size)
+            return RouteResult(r.route, r.frontier, r.kept, csr)
+        selected = kernels.route_select(
+            mass, prev=previous if c.route_persistence else None, persistence=c.route_persistence,
+            target=c.mass_target, keep=c.keep, sink_blocks=self._sink_blocks(state))
+        return self._csr_result(selected, tokens, layout)
 
     def _exact_route(self, state, q, k, softmax_scale, mass=None):
         c = self.config
         if mass is None:
             mass = _block_attention_mass(q, k, None, c.block_size, scale=softmax_scale)
-        result = kernels.route_select(mass, target=c.mass_target, keep=c.keep,
-                                      sink_blocks=self._sink_blocks(state))
-        return self._result_from_csr(state, result, q.shape[1])
+        selected = kernels.route_select(mass, target=c.mass_target, keep=c.keep,
+                                        sink_blocks=self._sink_blocks(state))
+        return self._csr_result(selected, q.shape[1], state.get("layout"))
 
-    def _install_route(self, state, result, tokens):
-        block_mask = result.get("block_mask")
-        if block_mask is None:
-            block_mask = _build_block_mask(result["route"], tokens, self.config.block_size)
-        state.update({
-            "route": result["route"],
-            "frontier": result.get("frontier"),
-            "kept": result.get("kept"),
-            "block_mask": block_mask,
-        })
+    def _add_first_frame_sink(self, state, result):
+        """Force the first latent frame's key blocks on in every row
+        (``flex.py:550-566``); the selection kernels do this themselves, this
+        helper serves routes built elsewhere."""
+        sink = self._sink_blocks(state)
+        if sink == 0:
+            return result
+        route = result["route"].clone()
+        route[..., :sink] = True
+        layout = state.get("layout")
+        frontier = (frontier_mask(route, layout.neighbors(route.device)) if layout is not None
+                    else result.get("frontier"))
+        return {**dict(result), "route": route, "frontier": frontier, "kept": None,
+                "block_mask": None}
+
+    def _dense_with_mass(self, q, k, v, softmax_scale, dense_only):
+        """Dense output plus its exact block mass from one attention pass; SDPA
+        and no mass (computed later from q, k) for inputs that kernel does
+        not take."""
+        output, mass = _dense_and_mass(q, k, v, self.config.block_size, softmax_scale)
+        if output is None:
+            return self.dense(q, k, v, **dense_only), None
+        return output, mass[0]
 
     def _spatial_layout(self, grid, tokens):
-        if not self.config.spatial_reorder:
+        c = self.config
+        if not c.spatial_reorder or grid is None or math.prod(grid) != tokens:
             return None
-        if grid is None or math.prod(grid) != tokens:
-            return None
-        key = (tuple(grid), self.config.block_size, self.config.spatial_microtile_tokens)
-        if key not in self.spatial_layouts:
-            self.spatial_layouts[key] = build_spatial_layout(
-                grid, self.config.block_size, self.config.spatial_microtile_tokens)
-        return self.spatial_layouts[key]
+        key = (tuple(grid), c.block_size, c.spatial_microtile_tokens)
+        layout = self.spatial_layouts.get(key)
+        if layout is None:
+            layout = build_spatial_layout(grid, c.block_size, c.spatial_microtile_tokens)
+            self.spatial_layouts[key] = layout
+        return layout
 
-    def _prefetch_sampled_route(self, state, q, k, step, softmax_scale, phase="sampled_update"):
-        stream = self.route_streams.setdefault(q.device, torch.cuda.Stream(device=q.device))
-        attention_done = torch.cuda.Event()
-        attention_done.record(torch.cuda.current_stream(q.device))
-        stream.wait_event(attention_done)
-        with torch.cuda.stream(stream):
-            q.record_stream(stream)
-            k.record_stream(stream)
+    def _launch_side_route(self, state, q, k, step, softmax_scale):
+        """Start the sampled route on the device's route stream after the work
+        already queued on the current stream; adopted by the next call."""
+        device = q.device
+        side = self.route_streams.get(device)
+        if side is None:
+            side = self.route_streams[device] = torch.cuda.Stream(device=device)
+        queued = torch.cuda.Event()
+        queued.record(torch.cuda.current_stream(device))
+        side.wait_event(queued)
+        with torch.cuda.stream(side):
+            q.record_stream(side)
+            k.record_stream(side)
             result = self._sampled_route(state, q, k, softmax_scale)
+            if not isinstance(result, RouteResult):
+                result = self._as_result(result, q.shape[1])
             ready = torch.cuda.Event()
-            ready.record(stream)
-        state["pending"] = {
-            "route": result["route"],
-            "frontier": result.get("frontier"),
-            "kept": result.get("kept"),
-            "block_mask": result["block_mask"],
-            "source_step": step,
-            "ready": ready,
-        }
-        self.phase_counts[phase] += 1
+            ready.record(side)
+        state.pending = PendingRoute(result, step, ready)
 
     def install_route(self, route, *, attention_id, branch, tokens, heads, head_dim, device,
                       grid=None, step=0):
@@ -436,31 +573,15 @@ class FlexReuseBackend:
         route = route.to(device=device, dtype=torch.bool)
         key = (attention_id, branch, tokens, heads, head_dim, route.device,
                layout.signature if layout is not None else None)
-        state = {"route": route, "frontier": None, "step": step, "layout": layout, "grid": grid,
-                 "kept": route.reshape(route.shape[0], -1).sum(-1),
-                 "block_mask": _build_block_mask(route, tokens, self.config.block_size)}
-        if layout is not None:
-            state["frontier"] = frontier_mask(route, layout.neighbors(route.device))
-        self._update_dispatch(state)
+        state = RouteState(step=step, layout=layout, grid=grid)
+        frontier = (frontier_mask(route, layout.neighbors(route.device))
+                    if layout is not None else None)
+        self._install(state, RouteResult(route, frontier,
+                                         route.reshape(route.shape[0], -1).sum(-1),
+                                         _build_block_mask(route, tokens,
+                                                           self.config.block_size)), tokens)
         self.state[key] = state
-        return state
-
-    def profile_summary(self):
-        active = [s for s in self.state.values() if s.get("route") is not None]
-        keep = [s.get("keep") for s in active] + [
-            s["keep"] for s in self.finished_routes if s["keep"] is not None]
-        frontier = [s.get("frontier_fraction") for s in active] + [
-            s["frontier_fraction"] for s in self.finished_routes
-            if s["frontier_fraction"] is not None]
-        return {
-            "phase_counts": dict(self.phase_counts),
-            "active_routes": len(active),
-            "released_routes": len(self.finished_routes),
-            "mean_route_keep": sum(keep) / len(keep) if keep else None,
-            "mean_frontier_fraction": sum(frontier) / len(frontier) if frontier else None,
-            "dense_dispatched_routes": sum(bool(s.get("dense")) for s in self.state.values())
-            + sum(s["dense"] for s in self.finished_routes),
-        }
+        return self.state[key]
 
     # ------------------------------------------------------------------ call
     def _dense_call(self, q, k, v, **kw):
@@ -477,6 +598,24 @@ class FlexReuseBackend:
             return None
         return self._spatial_layout(grid, tokens)
 
+    def _plan(self, key, step):
+        """The action for this call: "bootstrap", "dense", "exact_refresh",
+        "sampled_update" (inline) or "reuse" / "reuse+prefetch"."""
+        c = self.config
+        state = self.state.get(key)
+        if step == 0 or state is None:
+            return "bootstrap"
+        self._adopt_pending(state)
+        if state.dense:
+            return "dense"
+        age = step - state.step
+        if c.update_interval > 0 and age >= c.update_interval and not self._final_step(step):
+            return "exact_refresh"
+        if (c.sampled_update_interval > 0 and age >= c.sampled_update_interval
+                and self._before_last_step(step)):
+            return "reuse+prefetch" if c.prefetch_sampled_update else "sampled_update"
+        return "reuse"
+
     def __call__(self, q, k, v, q_lens=None, k_lens=None, dropout_p=0.0, softmax_scale=None,
                  q_scale=None, causal=False, window_size=(-1, -1), deterministic=False,
                  dtype=torch.bfloat16, version=None, **kwargs):
@@ -484,122 +623,105 @@ class FlexReuseBackend:
         # prologue's output, see packed_layout_for); not part of the
         # reference's signature, which swallows unknown keywords.
         packed = kwargs.pop("packed_layout", None)
-        dense_kw = dict(q_lens=q_lens, k_lens=k_lens, dropout_p=dropout_p,
-                        softmax_scale=softmax_scale, q_scale=q_scale, causal=causal,
-                        window_size=window_size, deterministic=deterministic, dtype=dtype,
-                        version=version, **kwargs)
+        caller_kw = dict(q_lens=q_lens, k_lens=k_lens, dropout_p=dropout_p,
+                         softmax_scale=softmax_scale, q_scale=q_scale, causal=causal,
+                         window_size=window_size, deterministic=deterministic, dtype=dtype,
+                         version=version, **kwargs)
 
-        def dense_unpacked():
-            # dense attention is order-equivariant: restore a packed result
-            out = self._dense_call(q, k, v, **dense_kw)
+        def as_called():
+            # dense attention commutes with a token permutation: restore a
+            # packed result to the caller's order
+            out = self._dense_call(q, k, v, **caller_kw)
             return packed.restore(out.contiguous()) if packed is not None else out
 
-        supported = (q.shape[0] == 1 and q.shape[1] == k.shape[1] and dropout_p == 0
-                     and not causal and window_size == (-1, -1))
-        if not supported:
-            return dense_unpacked()
-
+        self_attention = q.shape[0] == 1 and q.shape[1] == k.shape[1]
+        if not (self_attention and dropout_p == 0 and not causal and window_size == (-1, -1)):
+            return as_called()
         attention_id, step, branch, grid = self._context()
         if self.config.first_layer_dense and attention_id == 0:
-            self.phase_counts["first_layer_dense"] += 1
-            return dense_unpacked()
+            self.log.hit("first_layer_dense")
+            return as_called()
         layout = self._spatial_layout(grid, q.shape[1])
         if self.config.spatial_reorder and layout is None:
-            return dense_unpacked()
+            return as_called()
         if packed is not None and (layout is None or packed.signature != layout.signature):
             q, k, v = (packed.restore(x.contiguous()) for x in (q, k, v))
             packed = None
 
         output_dtype = q.dtype
-        q = q.to(dtype)
-        k = k.to(dtype)
-        v = v.to(dtype)
+        q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
         if q_scale is not None:
             q = q * q_scale
         if layout is not None and packed is None:
             q, k, v = layout.reorder_qkv(q, k, v)
+        key = (attention_id, branch, q.shape[1], q.shape[2], q.shape[3], q.device,
+               layout.signature if layout is not None else None)
+        dense_kw = dict(dropout_p=0.0, softmax_scale=softmax_scale, q_scale=None, causal=False,
+                        window_size=(-1, -1), dtype=dtype)
 
-        def finish(output):
+        def unpacked(output):
             if layout is not None:
                 output = layout.restore(output)
             return output.to(output_dtype)
 
-        key = (attention_id, branch, q.shape[1], q.shape[2], q.shape[3], q.device,
-               layout.signature if layout is not None else None)
-        dense_only = dict(dropout_p=0.0, softmax_scale=softmax_scale, q_scale=None,
-                          causal=False, window_size=(-1, -1), dtype=dtype)
-        if step == 0 or key not in self.state:
-            state = {"route": None, "frontier": None, "block_mask": None, "step": step,
-                     "layout": layout, "grid": grid}
-            if self.config.bootstrap_mode == "exact":
-                output, mass = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
-                self.state[key] = state
-                self._install_route(state, self._exact_route(state, q, k, softmax_scale, mass),
-                                    q.shape[1])
-                self._update_dispatch(state)
-                self.phase_counts["dense_bootstrap"] += 1
-            else:
-                output = self.dense(q, k, v, **dense_only)
-                self.state[key] = state
-                if (self.config.prefetch_sampled_bootstrap
-                        and (self.config.total_steps is None
-                             or step < self.config.total_steps - 1)):
-                    self._prefetch_sampled_route(state, q, k, step, softmax_scale,
-                                                 phase="sampled_bootstrap")
-                else:
-                    self._install_route(state, self._sampled_route(state, q, k, softmax_scale),
-                                        q.shape[1])
-                    self._update_dispatch(state)
-                    self.phase_counts["sampled_bootstrap"] += 1
-            if self._is_final_step(step):
-                self._release_route(key, self.state[key])
-            return finish(output)
+        action = self._plan(key, step)
+        if action == "bootstrap":
+            output = self._bootstrap(key, step, layout, grid, q, k, v, softmax_scale, dense_kw)
+        elif action == "dense":
+            self.log.hit("dense_dispatch")
+            output = self.dense(q, k, v, **dense_kw)
+        elif action == "exact_refresh":
+            state = self.state[key]
+            output, mass = self._dense_with_mass(q, k, v, softmax_scale, dense_kw)
+            self._install(state, self._exact_route(state, q, k, softmax_scale, mass), q.shape[1],
+                          step)
+            self.log.hit("exact_refresh")
+        else:
+            state = self.state[key]
+            output = None
+            if action == "sampled_update":
+                state.block_mask = None
+                self._install(state, self._sampled_route(state, q, k, softmax_scale), q.shape[1],
+                              step)
+                self.log.hit("sampled_update")
+                if state.dense:
+                    self.log.hit("dense_dispatch")
+                    output = self.dense(q, k, v, **dense_kw)
+            if output is None:
+                # the output store writes raster order (the unpack is folded in)
+                raster = _flex_output(q, k, v, state.block_mask, self.config.block_size,
+                                      self.config.compile_kernel, scale=softmax_scale,
+                                      out_rows=(layout.permutation(q.device)
+                                                if layout is not None else None))
+                self.log.hit("sparse_reuse")
+                if action == "reuse+prefetch":
+                    state.block_mask = None
+                    self._launch_side_route(state, q, k, step, softmax_scale)
+                    self.log.hit("sampled_update")
+                if self._final_step(step):
+                    self._release(key)
+                return raster.to(output_dtype)
+        if self._final_step(step):
+            self._release(key)
+        return unpacked(output)
 
-        state = self.state[key]
-        self._activate_pending_route(state)
-        if state.get("dense"):
-            self.phase_counts["dense_dispatch"] += 1
-            output = self.dense(q, k, v, **dense_only).to(output_dtype)
-            if self._is_final_step(step):
-                self._release_route(key, state)
-            return finish(output)
-        if (self.config.update_interval > 0
-                and (step - state["step"]) >= self.config.update_interval
-                and not self._is_final_step(step)):
-            output, mass = self._dense_for_exact_route(q, k, v, softmax_scale, dense_only)
-            self._install_route(state, self._exact_route(state, q, k, softmax_scale, mass),
-                                q.shape[1])
-            state["step"] = step
-            self._update_dispatch(state)
-            self.phase_counts["exact_refresh"] += 1
-            return finish(output)
-
-        sampled_update_due = (
-            self.config.sampled_update_interval > 0
-            and (step - state["step"]) >= self.config.sampled_update_interval
-            and (self.config.total_steps is None or step < self.config.total_steps - 1))
-        if sampled_update_due and not self.config.prefetch_sampled_update:
-            state["block_mask"] = None
-            self._install_route(state, self._sampled_route(state, q, k, softmax_scale), q.shape[1])
-            state["step"] = step
-            self._update_dispatch(state)
-            self.phase_counts["sampled_update"] += 1
-            if state.get("dense"):
-                self.phase_counts["dense_dispatch"] += 1
-                return finish(self.dense(q, k, v, **dense_only))
-
-        # The sparse output goes straight back to raster order (no unpack pass).
-        output = _flex_output(q, k, v, state["block_mask"], self.config.block_size,
-                              self.config.compile_kernel, scale=softmax_scale,
-                              out_rows=layout.permutation(q.device) if layout is not None
-                              else None)
-        self.phase_counts["sparse_reuse"] += 1
-        if self.config.prefetch_sampled_update and sampled_update_due:
-            state["block_mask"] = None
-            self._prefetch_sampled_route(state, q, k, step, softmax_scale)
-        if self._is_final_step(step):
-            self._release_route(key, state)
-        return output.to(output_dtype)
+    def _bootstrap(self, key, step, layout, grid, q, k, v, softmax_scale, dense_kw):
+        """Step 0 (or a new key): dense output plus the first route, exact
+        from the same attention pass or sampled (``flex.py:706-762``)."""
+        state = RouteState(step=step, layout=layout, grid=grid)
+        self.state[key] = state
+        if self.config.bootstrap_mode == "exact":
+            output, mass = self._dense_with_mass(q, k, v, softmax_scale, dense_kw)
+            self._install(state, self._exact_route(state, q, k, softmax_scale, mass), q.shape[1])
+            self.log.hit("dense_bootstrap")
+            return output
+        output = self.dense(q, k, v, **dense_kw)
+        if self.config.prefetch_sampled_bootstrap and self._before_last_step(step):
+            self._launch_side_route(state, q, k, step, softmax_scale)
+        else:
+            self._install(state, self._sampled_route(state, q, k, softmax_scale), q.shape[1])
+        self.log.hit("sampled_bootstrap")
+        return output
 
 
 def install_flex_reuse(config=None):

@@ -145,3 +145,61 @@ def test_profile_summary_shape():
     assert set(summary) == {"phase_counts", "active_routes", "released_routes",
                             "mean_route_keep", "mean_frontier_fraction",
                             "dense_dispatched_routes"}
+
+
+def _sdpa(q, k, v):
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+
+
+def test_sampled_update_can_switch_route_to_dense_on_cpu(monkeypatch):
+    """The reference's CPU test (tests/test_flex_route_update.py:41-73): an
+    injected dict state, a substituted route producer returning a dict, and
+    the dense switch at keep >= threshold, all without a GPU."""
+    monkeypatch.setattr(flex_module, "routing_context",
+                        lambda include_grid=False: (1, 1, 0, None) if include_grid
+                        else (1, 1, 0))
+    monkeypatch.setattr(flex_module, "_build_block_mask", lambda *args: object())
+    q = torch.randn(1, 8, 1, 4)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    backend = FlexReuseBackend(FlexReuseConfig(sampled_update_interval=1,
+                                               prefetch_sampled_update=False,
+                                               dense_route_threshold=.75, total_steps=3))
+    backend.state[(1, 0, 8, 1, 4, q.device, None)] = {
+        "route": torch.eye(1, dtype=torch.bool), "block_mask": object(), "step": 0,
+        "dense": False}
+    monkeypatch.setattr(backend, "_sampled_route",
+                        lambda state, query, key, scale: {
+                            "route": torch.ones(1, 1, 1, dtype=torch.bool), "frontier": None})
+    output = backend(q, k, v, dtype=torch.float32)
+    torch.testing.assert_close(output, _sdpa(q, k, v))
+    state = backend.state[next(iter(backend.state))]
+    assert state["dense"] is True
+    assert state["route"] is None and state["block_mask"] is None
+    assert state["keep"] == 1.0 and state["step"] == 1
+    assert backend.phase_counts["dense_dispatch"] == 1
+    assert backend.phase_counts["sampled_update"] == 1
+    assert "pending" not in state
+
+
+def test_dense_state_is_released_at_the_final_step(monkeypatch):
+    """A dense-dispatched route keeps answering with SDPA and is released at
+    the last step; the summary counts it among the released routes."""
+    step = {"value": 1}
+    monkeypatch.setattr(flex_module, "routing_context",
+                        lambda include_grid=False: (2, step["value"], 1, None))
+    q = torch.randn(1, 8, 2, 4)
+    backend = FlexReuseBackend(FlexReuseConfig(total_steps=3, dense_route_threshold=0.5))
+    backend.state[(2, 1, 8, 2, 4, q.device, None)] = {"dense": True, "keep": 0.8, "step": 0}
+    torch.testing.assert_close(backend(q, q, q, dtype=torch.float32), _sdpa(q, q, q))
+    assert len(backend.state) == 1
+    step["value"] = 2
+    torch.testing.assert_close(backend(q, q, q, dtype=torch.float32), _sdpa(q, q, q))
+    assert backend.state == {}
+    summary = backend.profile_summary()
+    assert summary["phase_counts"]["dense_dispatch"] == 2
+    assert summary["released_routes"] == 1 and summary["active_routes"] == 0
+    assert summary["dense_dispatched_routes"] == 1
+    assert summary["mean_route_keep"] == 0.8
+    assert backend.finished_routes == [{"keep": 0.8, "frontier_fraction": None, "dense": True}]
