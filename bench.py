@@ -52,6 +52,11 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("bsa", "reference"), default="bsa")
+    p.add_argument("--workload", choices=("layer", "forward5"), default="layer",
+                   help="layer: config-4 attention layer (default); forward5: config-5 "
+                        "five-step Wan2.1-14B forward")
+    p.add_argument("--layers", type=int, default=0,
+                   help="forward5 only: fewer transformer layers (0 = the model's 40)")
     p.add_argument("--heads", type=int, default=40, help="heads (40 = config 4; fewer for profiling)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -430,6 +435,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "forward5":
+        return run_forward5(args)
 
     import torch.distributed as dist
 
@@ -642,6 +649,134 @@ def main(argv=None):
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# config 5: 5-step Wan2.1-14B forward
+# ----------------------------------------------------------------------------
+
+FORWARD5_FLEX = dict(bootstrap_mode="sampled", prefetch_sampled_bootstrap=True,
+                     sampled_update_interval=2, prefetch_sampled_update=False, route_samples=16,
+                     route_persistence=0.5, mass_target=0.95, keep=0.625,
+                     dense_route_threshold=0.58, spatial_reorder=True, total_steps=5)
+
+
+def run_forward5(args):
+    """Config 5: five denoising steps of a random-init Wan2.1-14B (40 layers,
+    dim 5120, 57,600 tokens, text 512 x 4096), CFG on, through the repo's
+    frontend (``wan_model``) on 1-8 GPUs: CFG branches on two rank groups,
+    tokens sequence-parallel inside a group, self-attention head-parallel.
+    Three runs of the same generation: dense SDPA attention; the
+    ``flex_reuse`` backend with the reference's recommended flags
+    (``README.md:46-54``: sampled bootstrap, sampled update every 2 steps,
+    dense dispatch at keep >= 0.58); and the same backend with the dense
+    threshold off, so every route after layer 0 / step 0 runs sparse.  Each is
+    warmed up with one step, then timed from the first transformer call to the
+    last scheduler update with CUDA events (max over ranks)."""
+    import torch.distributed as dist
+
+    from dit_sparse_atten_b200 import _native, parallel, wan_model
+    from dit_sparse_atten_b200.context import reset_runtime_state
+    from dit_sparse_atten_b200.dense import DenseBackend
+    from dit_sparse_atten_b200.flex import FlexReuseBackend, FlexReuseConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    _native.load_library()
+    cfg = wan_model.WanConfig(layers=args.layers) if args.layers else wan_model.WAN_14B
+    grid = (16, 45, 80)
+    plan = parallel.make_plan(world, rank, cfg.heads, batch=2)
+    group = parallel.new_groups(plan) if world > 1 else None
+    pair = (wan_model.pair_groups(world, plan.group_size)
+            if world > 1 and plan.cfg_groups == 2 else None)
+    P = plan.group_size
+    shard = wan_model.SequenceShard(group if P > 1 else None, P, plan.group_rank)
+    weights = wan_model.WanWeights(cfg, device, seed=0)
+    model = wan_model.WanTransformer(weights, grid, shard, wan_model.fused_prologue(cfg.heads,
+                                                                                   cfg.eps))
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    latent = torch.randn((cfg.in_channels, grid[0], 2 * grid[1], 2 * grid[2]), generator=g,
+                         device=device)
+    text = [torch.randn((1, cfg.text_tokens, cfg.text_dim), generator=g, device=device,
+                        dtype=torch.bfloat16) for _ in range(2)]
+    rows = wan_model.patchify(latent, cfg)[model.rows].contiguous()
+    branches = plan.branches(2)
+    contexts = {b: model.context(text[b]) for b in branches}
+    combine = wan_model.CfgCombine(5.0, pair_group=pair)
+
+    def timed(make_backend, steps):
+        backend = make_backend()
+        reset_runtime_state()
+
+        def attention(q, k, v):
+            return parallel.head_parallel_attention(q, k, v, lambda a, b, c: backend(a, b, c),
+                                                    shard.group, P)
+        step_ms = []
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        marks[0].record()
+        out = wan_model.denoise(model, rows, contexts, attention, combine, steps=steps,
+                                on_step=lambda i: marks[i + 1].record())
+        torch.cuda.synchronize()
+        _native.check_device_errors()
+        step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(steps)]
+        total = torch.tensor([sum(step_ms)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        summary = backend.profile_summary() if hasattr(backend, "profile_summary") else None
+        return float(total[0]) / 1e3, step_ms, summary, bool(torch.isfinite(out).all())
+
+    variants = {
+        "dense": lambda: DenseBackend(),
+        "flex_reuse": lambda: FlexReuseBackend(FlexReuseConfig(**FORWARD5_FLEX),
+                                               process_group=group),
+        "flex_reuse_all_sparse": lambda: FlexReuseBackend(
+            FlexReuseConfig(**{**FORWARD5_FLEX, "dense_route_threshold": None}),
+            process_group=group),
+    }
+    results = {}
+    with ClockSampler(local) as clocks:
+        for name, make in variants.items():
+            timed(make, 1)                     # warm-up: one step, fresh state
+            seconds, step_ms, summary, finite = timed(make, 5)
+            results[name] = {"forward_5step_s": seconds,
+                             "step_ms_rank0": [round(x, 1) for x in step_ms],
+                             "finite": finite}
+            if summary is not None:
+                results[name]["routes"] = {k: summary[k] for k in
+                                           ("phase_counts", "mean_route_keep",
+                                            "dense_dispatched_routes", "released_routes")}
+    line = {
+        "metric": METRIC, "value": results["flex_reuse"]["forward_5step_s"], "unit": "s",
+        "n_gpus": world, "steps": 5, "warmup": 1, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init Wan2.1-14B weights, seeded latent and text)",
+        "config": {"workload": "config5_wan14b_5step_forward: 57,600 tokens, CFG on, "
+                               f"{cfg.layers} layers, dim {cfg.dim}, FFN {cfg.ffn}, "
+                               f"{cfg.heads} heads, text {cfg.text_tokens} x {cfg.text_dim}",
+                   "parallelism": f"{plan.cfg_groups} CFG group(s) x {P}-way sequence/head "
+                                  "parallel (Ulysses all-to-all, NCCL)",
+                   "params": weights.parameter_count(),
+                   "flex_reuse_flags": FORWARD5_FLEX},
+        "variants": results,
+        "speedup_vs_dense": {k: results["dense"]["forward_5step_s"] / v["forward_5step_s"]
+                             for k, v in results.items() if k != "dense"},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 

@@ -318,7 +318,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // constant), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
 // coefficients were fitted for this kernel with the Remez exchange algorithm
 // (minimax relative error 7.5e-5 on [-1/2, 1/2], far below the 2^-8 rounding
-// of the bf16 probabilities); 2^n is added to the exponent bits.  Inputs are
+// of the bf16 probabilities; fit_exp2_poly.py next to this file derives them);
+// 2^n is added to the exponent bits.  Inputs are
 // clamped to >= -126, so results below 2^-126 come out as ~2^-126 instead of 0.
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23

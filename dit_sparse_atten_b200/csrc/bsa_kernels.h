@@ -158,6 +158,11 @@ struct AttnArgs {
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args,
                              cudaStream_t stream);
+// The 128-token-block kernel that gives each CTA two adjacent query blocks
+// (attention_pair.cu); launch_attention uses it for block == 128.
+cudaError_t launch_attention_pair(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                  const CUtensorMap& tm_v, const AttnArgs& args,
+                                  cudaStream_t stream);
 // mass [B, H, Kb, Kb] from block_lse [B, H, Kb, T] and the natural-log row LSE
 // [B, H, T] of the same dense pass (128-token blocks).
 cudaError_t launch_block_mass(const float* block_lse, const float* lse, int64_t batch,
