@@ -519,13 +519,13 @@ cudaError_t launch_block_mass(const float* block_lse, const float* lse, int64_t 
 cudaError_t launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                              const AttnArgs& a, cudaStream_t stream) {
   if (a.batch == 0 || a.heads == 0 || a.q_blocks == 0) return cudaSuccess;
-  // BSA_ATTENTION_KERNEL=single selects the one-query-block kernel for
-  // 128-token blocks (kept for comparison); the default is the pair kernel.
-  static const bool single = [] {
+  // BSA_ATTENTION_KERNEL=pair selects the two-query-block kernel for
+  // 128-token blocks (attention_pair.cu); the default is the one-block kernel.
+  static const bool pair = [] {
     const char* v = getenv("BSA_ATTENTION_KERNEL");
-    return v != nullptr && strcmp(v, "single") == 0;
+    return v != nullptr && strcmp(v, "pair") == 0;
   }();
-  if (a.block == 128 && !single) return launch_attention_pair(tq, tk, tv, a, stream);
+  if (a.block == 128 && pair) return launch_attention_pair(tq, tk, tv, a, stream);
   if (a.block_lse != nullptr) {
     if (a.block == 128) return launch_bk<128, true>(tq, tk, tv, a, stream);
     return cudaErrorInvalidValue;

@@ -22,11 +22,12 @@
 // order "shared ascending, then its own ascending"; the online softmax makes
 // the result independent of that order up to rounding.
 //
-// Roles (320 threads):
-//   warp 8   producer: builds the schedule by walking the two CSR rows, puts
-//            each step's (tile mask, key block) into a ring of step records,
-//            and TMA-loads K_s and V_{s-1} into a ring of 32 KB slots in the
-//            order the MMA issuer first uses them;
+// Roles (352 threads):
+//   warp 10  scheduler: builds the schedule by walking the two CSR rows and
+//            puts each step's (tile mask, key block) into a ring of step
+//            records that runs ahead of the two consumers below;
+//   warp 8   loader: TMA-loads K_s and V_{s-1} into a ring of 32 KB slots in
+//            the order the MMA issuer first uses them;
 //   warp 9   TMEM owner; one thread TMA-loads both Q tiles and issues every
 //            MMA in one stream: per step, for each tile t in the step,
 //            O_t += P_t V_{prev} (if tile t had the previous step) then
@@ -54,12 +55,32 @@ namespace {
 
 using namespace attn;
 
-constexpr int kPairThreads = 320;
-constexpr int kPairProducerWarp = 8;
-constexpr int kPairMmaWarp = 9;
+// Softmax warps per (tile, TMEM lane quarter): 1 (a thread owns a whole
+// 128-column row) or 2 (column halves; the halves meet once per block to
+// agree on the row max).
+#ifndef BSA_PAIR_HALVES
+#define BSA_PAIR_HALVES 2
+#endif
+constexpr int kHalves = BSA_PAIR_HALVES;
+static_assert(kHalves == 1 || kHalves == 2, "one or two softmax warps per row quarter");
+constexpr int kSoftWarps = 8 * kHalves;
+constexpr int kColsPerThread = 128 / kHalves;
+// Warpgroups: the softmax warps (tile 0, then tile 1), then one control
+// warpgroup: loader, MMA issuer, scheduler and one idle warp.  At launch every
+// thread has kLaunchRegs registers; the control warpgroup gives some back and
+// the softmax warpgroups take them, never more than the launch total.
+constexpr int kPairThreads = 32 * (kSoftWarps + 4);
+constexpr int kPairProducerWarp = kSoftWarps;
+constexpr int kPairMmaWarp = kSoftWarps + 1;
+constexpr int kPairSchedWarp = kSoftWarps + 2;
+constexpr uint32_t kLaunchRegs = kHalves == 1 ? 168 : 96;
+constexpr uint32_t kSoftmaxRegs = kHalves == 1 ? 200 : 104;
+constexpr uint32_t kControlRegs = kHalves == 1 ? 104 : 64;
+static_assert(kSoftWarps * 32 * kSoftmaxRegs + 128 * kControlRegs <= kPairThreads * kLaunchRegs,
+              "register split must stay within the launch total");
 constexpr int kPairHeadDim = 128;
-constexpr int kPairSlots = 5;
-constexpr int kStepRing = 8;
+constexpr int kPairSlots = kHalves == 1 ? 5 : 4;
+constexpr int kStepRing = 16;
 constexpr uint32_t kTmemS = 0;      // + 128 * tile
 constexpr uint32_t kTmemO = 256;    // + 128 * tile
 // Of every 8 column pairs of a full key block, this many take their
@@ -68,13 +89,23 @@ constexpr uint32_t kTmemO = 256;    // + 128 * tile
 #define BSA_PAIR_EMULATED_PAIRS 0
 #endif
 constexpr int kPairEmulated = BSA_PAIR_EMULATED_PAIRS;
+// Chunks of the S row kept in registers between the max and exponential
+// passes (the rest are read from TMEM again).
+#ifndef BSA_PAIR_KEPT_CHUNKS
+#define BSA_PAIR_KEPT_CHUNKS (4 / BSA_PAIR_HALVES)
+#endif
+constexpr int kPairKept = BSA_PAIR_KEPT_CHUNKS;
 
 struct PairLayout {
   static constexpr int kPanel = 128 * 128;                 // one 64-column panel: 16 KB
   static constexpr int kSlotBytes = 2 * kPanel;            // a 128 x 128 bf16 tile
   static constexpr int kQOff = 0;                          // Q_0, Q_1
   static constexpr int kRingOff = 2 * kSlotBytes;
-  static constexpr int kBarOff = kRingOff + kPairSlots * kSlotBytes;
+  // Row exchange between the two halves of a row: [parity][tile][half][row]
+  // floats for the row max, and the same for the block sums (dense mass).
+  static constexpr int kXOff = kRingOff + kPairSlots * kSlotBytes;
+  static constexpr int kXBytes = kHalves == 2 ? 2 * 2 * 2 * 2 * 128 * 4 : 0;
+  static constexpr int kBarOff = kXOff + kXBytes;
   static constexpr int kBarBytes = 640;
   static constexpr int kUsed = kBarOff + kBarBytes;
 };
@@ -235,11 +266,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int r = 0; r < kStepRing; ++r) {
       mbar_init(&bar->step_full[r], 1);
-      mbar_init(&bar->step_empty[r], 1);
+      mbar_init(&bar->step_empty[r], 2);   // the loader and the MMA issuer
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar->s_full[t], 1);
-      mbar_init(&bar->p_full[t], 128);
+      mbar_init(&bar->p_full[t], 128 * kHalves);
       mbar_init(&bar->kb_full[t], 1);
       mbar_init(&bar->o_final[t], 1);
     }
@@ -255,13 +286,36 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
-
-  if (warp == kPairProducerWarp) {
-    // ------------------------------------------------------------ producer
+  // The register split sits at the top of the two role branches (not before
+  // a join), so each branch is compiled against its own budget.
+  if (warp >= kSoftWarps) {
+   setmaxnreg_dec<kControlRegs>();
+   if (warp == kPairSchedWarp) {
+    // ------------------------------------------------------------ scheduler
+    // Walks the two CSR rows and fills the step ring ahead of the loader and
+    // the MMA issuer (both consume every step record).
+    if (lane == 0 && any_work) {
+      ScheduleWalker walk{row0, row1, a.k_blocks, a.err_word};
+      for (int s = 0;; ++s) {
+        int info;
+        if constexpr (kDenseMass) {
+          info = s < a.k_blocks ? ((s << 2) | (has_tile1 ? 3 : 1)) : 0;
+        } else {
+          info = walk.next_step();
+        }
+        const int r = s % kStepRing;
+        if (!mbar_wait(&bar->step_empty[r], ((s / kStepRing) & 1) ^ 1, abort_flag, a.err_word))
+          break;
+        bar->step_info[r] = info;
+        mbar_arrive(&bar->step_full[r]);
+        if ((info & 3) == 0) break;
+      }
+    }
+   } else if (warp == kPairProducerWarp) {
+    // ------------------------------------------------------------ loader
     if (lane == 0 && any_work) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      ScheduleWalker walk{row0, row1, a.k_blocks, a.err_word};
       uint32_t armed = 0, armed_phase = 0;   // per slot: load issued / its parity
       int seq = 0;
       bool ok = true;
@@ -280,17 +334,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       };
       int prev_mask = 0, prev_kb = 0;
       for (int s = 0; ok; ++s) {
-        int info;
-        if constexpr (kDenseMass) {
-          info = s < a.k_blocks ? ((s << 2) | (has_tile1 ? 3 : 1)) : 0;
-        } else {
-          info = walk.next_step();
-        }
         const int r = s % kStepRing;
-        ok = mbar_wait(&bar->step_empty[r], ((s / kStepRing) & 1) ^ 1, abort_flag, a.err_word);
+        ok = mbar_wait(&bar->step_full[r], (s / kStepRing) & 1, abort_flag, a.err_word);
         if (!ok) break;
-        bar->step_info[r] = info;
-        mbar_arrive(&bar->step_full[r]);
+        const int info = bar->step_info[r];
+        mbar_arrive(&bar->step_empty[r]);
         const int mask = info & 3;
         const int kb = info >> 2;
         // First-use order of the issuer: V of the previous step before K of
@@ -310,7 +358,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (armed & (1u << s))
           mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
-  } else if (warp == kPairMmaWarp) {
+   } else if (warp == kPairMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && any_work) {
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
@@ -401,22 +449,32 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       umma_commit(&bar->drain);
       mbar_wait(&bar->drain, 0, &never, a.err_word);
     }
+   }
   } else {
+    setmaxnreg_inc<kSoftmaxRegs>();
     // ------------------------------------------------------------ softmax
-    const int t = warp >> 2;                   // tile
+    const int t = warp / (4 * kHalves);        // tile
     const int wq = warp & 3;                   // TMEM lane quarter
+    const int hf = (warp / 4) % kHalves;       // column half of the row (kHalves == 2)
     const int row = wq * 32 + lane;            // query row == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
     const int qb = qb0 + t;
     const int64_t token = static_cast<int64_t>(qb) * 128 + row;
     const int n = t ? row1.n : row0.n;
     const bool row_valid = (t == 0 || has_tile1) && token < a.tokens;
-    const uint32_t sbuf = tmem + lane_addr + kTmemS + t * 128;
-    const uint32_t obuf = tmem + lane_addr + kTmemO + t * 128;
+    // This thread's S columns, its P columns (bf16 pairs, half as many) and
+    // its O columns.
+    const uint32_t sbuf = tmem + lane_addr + kTmemS + t * 128 + hf * kColsPerThread;
+    const uint32_t pbuf = tmem + lane_addr + kTmemS + t * 128 + hf * (kColsPerThread / 2);
+    const uint32_t obuf = tmem + lane_addr + kTmemO + t * 128 + hf * kColsPerThread;
+    float* xmax = reinterpret_cast<float*>(smem + L::kXOff);            // [2][2][2][128]
+    float* xsum = xmax + 2 * 2 * 2 * 128;
+    auto xidx = [&](int parity, int half) { return ((parity * 2 + t) * 2 + half) * 128 + row; };
+    const uint32_t pair_bar = 1 + t * 4 + wq;  // named barrier of the row's two halves
     const float c = a.scale * kLog2e;
     const float2 c2 = make_float2(c, c);
     float m_run = -INFINITY;   // stabiliser (log2 units) the row's O and l are relative to
-    float l = 0.f;             // row sum relative to m_run
+    float l = 0.f;             // this thread's part of the row sum, relative to m_run
     bool ok = true;
     for (int j = 0; ok && j < n; ++j) {
       int kb = 0;
@@ -428,24 +486,31 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       ok = mbar_wait(&bar->s_full[t], j & 1, abort_flag, a.err_word);
       if (!ok) break;
       tc_fence_after();
-      const int64_t valid = a.tokens - static_cast<int64_t>(kb) * 128;
-      const bool partial = kTail && valid < 128;
-      uint32_t keep[kKeptChunks<128>][32];
-      const float mrow = row_max<128>(sbuf, partial, valid, keep) * c;
+      const int64_t valid = a.tokens - static_cast<int64_t>(kb) * 128 - hf * kColsPerThread;
+      const bool partial = kTail && valid < kColsPerThread;
+      uint32_t keep[kPairKept][32];
+      float mrow = row_max<kColsPerThread, kPairKept>(sbuf, partial, valid, keep) * c;
+      if constexpr (kHalves == 2) {
+        // Both halves' S columns are in registers now, so P may overwrite
+        // them after this barrier; the row max is the larger half's.
+        xmax[xidx(j & 1, hf)] = mrow;
+        named_bar_sync(pair_bar, 64);
+        mrow = fmaxf(mrow, xmax[xidx(j & 1, hf ^ 1)]);
+      }
       const bool need = mrow > m_run + kRescaleThreshold;
       const float m_used = need ? mrow : m_run;
       const float2 neg_m = make_float2(-m_used, -m_used);
       // With a partial block possible, every exponential stays on MUFU (one
       // code path for masked and full blocks).
-      const float2 rs = row_exp<128, kTail ? 0 : kPairEmulated>(sbuf, partial, valid, c2, neg_m,
-                                                                 keep);
+      const float2 rs = row_exp<kColsPerThread, kTail ? 0 : kPairEmulated, kPairKept>(
+          sbuf, partial, valid, c2, neg_m, keep, pbuf);
       // O_t holds the blocks before j relative to m_run; it is complete here
       // (its last PV was issued before this S, and s_full tracks both), and
       // PV of block j waits for p_full below.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         const float o_scale = need ? ex2_approx(m_run - m_used) : 1.f;
 #pragma unroll 1
-        for (int cc = 0; cc < kPairHeadDim / 32; ++cc) {
+        for (int cc = 0; cc < kColsPerThread / 32; ++cc) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(obuf + cc * 32, o);
           tmem_wait_ld();
@@ -458,10 +523,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       l = l * ex2_approx(m_run - m_used) + (rs.x + rs.y);   // m_run = -inf at j = 0: l = 0
       m_run = m_used;
       if constexpr (kDenseMass) {
-        if (row_valid) {
+        float block_sum = rs.x + rs.y;
+        if constexpr (kHalves == 2) {
+          xsum[xidx(j & 1, hf)] = block_sum;
+          named_bar_sync(pair_bar, 64);
+          block_sum = xsum[xidx(j & 1, 0)] + xsum[xidx(j & 1, 1)];
+        }
+        if (row_valid && hf == 0) {
           float* dst = a.block_lse + static_cast<int64_t>(kb) * a.tokens + token;
           dst[(static_cast<int64_t>(b) * a.heads + h) * a.k_blocks * a.tokens] =
-              m_used + __log2f(rs.x + rs.y);
+              m_used + __log2f(block_sum);
         }
       }
       tmem_wait_st();
@@ -469,6 +540,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_arrive(&bar->p_full[t]);
     }
     // ---------------------------------------------------------- epilogue
+    if constexpr (kHalves == 2) {
+      // Both halves used the same stabilisers: the row sum is the sum of parts.
+      named_bar_sync(pair_bar, 64);
+      xsum[xidx(0, hf)] = l;
+      named_bar_sync(pair_bar, 64);
+      l = xsum[xidx(0, 0)] + xsum[xidx(0, 1)];
+    }
     if (ok && n > 0) {
       ok = mbar_wait(&bar->o_final[t], 0, abort_flag, a.err_word);
       tc_fence_after();
@@ -484,9 +562,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     const float inv_l = (n > 0 && l > 0.f) ? 1.f / l : 0.f;
     __nv_bfloat16* out = a.out + b * a.out_stride_b + out_token * a.out_stride_t +
-                         h * a.out_stride_h;
+                         h * a.out_stride_h + hf * kColsPerThread;
 #pragma unroll 1
-    for (int cc = 0; cc < kPairHeadDim / 32; ++cc) {
+    for (int cc = 0; cc < kColsPerThread / 32; ++cc) {
       uint32_t o[32];
       if (ok && n > 0) {
         tmem_ld_32x32b_x32(obuf + cc * 32, o);
@@ -512,7 +590,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
     }
-    if (row_valid && a.lse != nullptr) {
+    if (row_valid && hf == 0 && a.lse != nullptr) {
       a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
           (n > 0 && l > 0.f) ? (m_run + __log2f(l)) * kLn2 : -INFINITY;
     }
@@ -541,6 +619,12 @@ cudaError_t launch_pair_impl(const CUtensorMap& tq, const CUtensorMap& tk, const
     // The layout needs kUsed bytes from a 1024-byte-aligned base.
     bytes = optin < L::kUsed + 1024 ? optin : L::kUsed + 1024;
     if (bytes < L::kUsed) return cudaErrorInvalidConfiguration;
+    // The register split inside the kernel assumes exactly kLaunchRegs per
+    // thread at launch; anything else could leave an increase waiting.
+    cudaFuncAttributes attr{};
+    e = cudaFuncGetAttributes(&attr, bsa_attention_pair_kernel<kDenseMass, kTail>);
+    if (e != cudaSuccess) return e;
+    if (attr.numRegs != static_cast<int>(kLaunchRegs)) return cudaErrorInvalidConfiguration;
     e = cudaFuncSetAttribute(bsa_attention_pair_kernel<kDenseMass, kTail>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;

@@ -72,19 +72,19 @@ constexpr int kKeptChunks = BK == 128 ? 2 : 1;
 // First pass: the row max (raw scores) of the BK-column S row at sbuf, all
 // chunks loaded at once; the last kKeptChunks chunks stay in `keep` (masked)
 // for the second pass.
-template <int BK>
+template <int BK, int kKeep = kKeptChunks<BK>>
 __device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t valid,
-                                         uint32_t (&keep)[kKeptChunks<BK>][32]) {
+                                         uint32_t (&keep)[kKeep][32]) {
   constexpr int kChunks = BK / 32;
-  constexpr int kFirst = kChunks - kKeptChunks<BK>;
-  uint32_t r[kFirst][32];
+  constexpr int kFirst = kChunks - kKeep;
+  uint32_t r[kFirst > 0 ? kFirst : 1][32];
   float m8[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) m8[q] = -INFINITY;
 #pragma unroll
   for (int k = 0; k < kFirst; ++k) tmem_ld_32x32b_x32(sbuf + k * 32, r[k]);
 #pragma unroll
-  for (int k = 0; k < kKeptChunks<BK>; ++k) tmem_ld_32x32b_x32(sbuf + (kFirst + k) * 32, keep[k]);
+  for (int k = 0; k < kKeep; ++k) tmem_ld_32x32b_x32(sbuf + (kFirst + k) * 32, keep[k]);
   tmem_wait_ld();
 #pragma unroll
   for (int k = 0; k < kFirst; ++k) {
@@ -93,7 +93,7 @@ __device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t va
     max_chunk(m8, r[k]);
   }
 #pragma unroll
-  for (int k = 0; k < kKeptChunks<BK>; ++k) {
+  for (int k = 0; k < kKeep; ++k) {
     reg_fence<32>(keep[k]);
     if (partial) mask_chunk(keep[k], (kFirst + k) * 32, valid);
     max_chunk(m8, keep[k]);
@@ -106,31 +106,34 @@ __device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t va
 // already read hold).  The first chunks are read from TMEM again (two buffers
 // alternate so a load overlaps the previous chunk's arithmetic); the kept
 // ones come from `keep`, already masked.  Returns the row's partial sums.
-template <int BK, int kEmulated>
+template <int BK, int kEmulated, int kKeep = kKeptChunks<BK>>
 __device__ __forceinline__ float2 row_exp(uint32_t sbuf, bool partial, int64_t valid, float2 c2,
                                           float2 neg_m,
-                                          const uint32_t (&keep)[kKeptChunks<BK>][32]) {
+                                          const uint32_t (&keep)[kKeep][32], uint32_t pbuf = ~0u) {
+  if (pbuf == ~0u) pbuf = sbuf;   // P of chunk k goes to columns pbuf + [16k, 16k + 16)
   constexpr int kChunks = BK / 32;
-  constexpr int kReload = kChunks - kKeptChunks<BK>;
+  constexpr int kReload = kChunks - kKeep;
   float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                    make_float2(0.f, 0.f)};
   uint32_t r[2][32];
-  tmem_ld_32x32b_x32(sbuf, r[0]);
-  tmem_wait_ld();
-  reg_fence<32>(r[0]);
+  if constexpr (kReload > 0) {
+    tmem_ld_32x32b_x32(sbuf, r[0]);
+    tmem_wait_ld();
+    reg_fence<32>(r[0]);
+  }
 #pragma unroll
   for (int k = 0; k < kReload; ++k) {
     if (k + 1 < kReload) tmem_ld_32x32b_x32(sbuf + (k + 1) * 32, r[(k + 1) & 1]);
     if (partial) mask_chunk(r[k & 1], k * 32, valid);
-    exp_chunk<kEmulated>(r[k & 1], c2, neg_m, acc, sbuf + k * 16);
+    exp_chunk<kEmulated>(r[k & 1], c2, neg_m, acc, pbuf + k * 16);
     if (k + 1 < kReload) {
       tmem_wait_ld();
       reg_fence<32>(r[(k + 1) & 1]);
     }
   }
 #pragma unroll
-  for (int k = 0; k < kKeptChunks<BK>; ++k)
-    exp_chunk<kEmulated>(keep[k], c2, neg_m, acc, sbuf + (kReload + k) * 16);
+  for (int k = 0; k < kKeep; ++k)
+    exp_chunk<kEmulated>(keep[k], c2, neg_m, acc, pbuf + (kReload + k) * 16);
   return __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
 }
 

@@ -128,6 +128,22 @@ __device__ __forceinline__ bool prior_timeout(const int* err_word) {
 }
 
 // ---------------------------------------------------------------------------
+// Register reallocation between warpgroups (setmaxnreg): all four warps of a
+// warpgroup execute the same instruction.  The block's registers at launch
+// (threads x registers per thread) must cover every warpgroup's new share, or
+// an increase waits for registers that never come: callers check the
+// kernel's register count on the host before launching.
+// ---------------------------------------------------------------------------
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+// ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), CTA-local destination, no multicast.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
