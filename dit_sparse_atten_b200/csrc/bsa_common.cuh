@@ -353,6 +353,16 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   return make_float2(__uint_as_float(b0), __uint_as_float(b1));
 }
 
+// bf16 round-to-nearest-even of two floats without the conversion unit:
+// t = x * (2^16 + 1), hi = t - (t - x) keeps the 8 leading significand bits
+// with ties to even (Veltkamp splitting; exact for |x| < 2^111).  Explicit _rn
+// operations: a fused multiply-add would break it.
+__device__ __forceinline__ float2 round2_bf16(float2 x) {
+  const float2 t = __fmul2_rn(x, make_float2(65537.f, 65537.f));
+  const float2 d = __ffma2_rn(x, make_float2(-1.f, -1.f), t);
+  return __ffma2_rn(d, make_float2(-1.f, -1.f), t);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

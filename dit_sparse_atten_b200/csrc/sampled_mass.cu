@@ -90,16 +90,6 @@ struct MassShape {
   static constexpr int kPairs = kCols / 2;
 };
 
-// bf16 round-to-nearest-even of two floats without the conversion unit:
-// t = x * (2^16 + 1), hi = t - (t - x) keeps the 8 leading significand bits
-// with ties to even (Veltkamp splitting; exact for |x| < 2^111, far above any
-// score here).  Explicit _rn operations: a fused multiply-add would break it.
-__device__ __forceinline__ float2 round2_bf16(float2 x) {
-  const float2 t = __fmul2_rn(x, make_float2(65537.f, 65537.f));
-  const float2 d = __ffma2_rn(x, make_float2(-1.f, -1.f), t);
-  return __ffma2_rn(d, make_float2(-1.f, -1.f), t);
-}
-
 // The same rounding through the conversion unit: one cvt.rn.bf16x2 packs both
 // values, two integer operations unpack them.  The kernel rounds the raw score
 // this way and the scaled score by Veltkamp splitting, which balances the
