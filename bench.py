@@ -492,19 +492,21 @@ def main(argv=None):
 
         chunk_events = []
 
-        def attend_chunk(qp, kp, vp, c):
-            # chunks run on alternating streams: events on the current one
+        def attend_chunk(qp, kp, vp, c, out, out_rows):
+            # the output store writes token order straight into the send
+            # buffer of the output all-to-all (the unpack folded in)
             cur = torch.cuda.current_stream(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(cur)
-            out_p = kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block)
+            kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block, out=out,
+                                           out_rows=out_rows)
             e1.record(cur)
             chunk_events.append((e0, e1))
             if c == pipe.chunks - 1:
                 # attention time of the step: first chunk start to last chunk end
                 attn_events.append((chunk_events[0][0], [e for _, e in chunk_events]))
                 chunk_events.clear()
-            return out_p
+            return None
 
     perm_dev = layout.permutation(device)
 
@@ -558,7 +560,10 @@ def main(argv=None):
         every = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(every, mine)
         rank_ms = {"step": [round(float(e[0]), 3) for e in every],
-                   "attention": [round(float(e[1]), 3) for e in every]}
+                   "attention": [round(float(e[1]), 3) for e in every],
+                   # step time not covered by this rank's attention span: the
+                   # exchange (and its row moves) left exposed
+                   "exposed": [round(float(e[0] - e[1]), 3) for e in every]}
         ms = max(float(e[0]) for e in every)
         attn_ms = max(float(e[1]) for e in every)
 
@@ -633,9 +638,10 @@ def main(argv=None):
         "stages": stages,
         **({"gpu_comparator": comparator} if comparator is not None else {}),
         "roofline": roofline,
-        # pack + attention per step (the unpack is folded into the attention's
-        # store); the chunked exchange runs gather, attention and unpack per chunk
-        "gpu_launches": args.steps * world * (3 * pipe.chunks if pipe is not None else 2),
+        # pack + attention per step (unpack folded into the store); the chunked
+        # exchange runs send gather, packed gather, attention and output
+        # scatter per chunk
+        "gpu_launches": args.steps * world * (4 * pipe.chunks if pipe is not None else 2),
         **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),
     }

@@ -22,6 +22,8 @@ SIGNATURES = {
     "bsa_version": ([], _I32),
     "bsa_last_error": ([], ctypes.c_char_p),
     "bsa_reorder_rows": ([_I32, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P], _I32),
+    "bsa_gather_scatter_rows": ([_I32, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
+                                _I32),
     "bsa_pack_boolean_rows": ([_P, _I64, _I32, _P, _P, _P], _I32),
     "bsa_route_select": ([_P, _P, _I64, _I32, _I32, _F32, _F32, _I32, _I32, _P, _P, _P, _P, _P],
                          _I32),

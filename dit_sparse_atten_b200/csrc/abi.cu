@@ -175,6 +175,26 @@ int bsa_reorder_rows(int32_t n_tensors, const void* const* src, void* const* dst
   return ok();
 }
 
+int bsa_gather_scatter_rows(int32_t n_tensors, const void* const* src, void* const* dst,
+                            const int32_t* src_rows, const int32_t* dst_rows, int64_t batch,
+                            int64_t rows, int64_t tokens_in, int64_t tokens_dst,
+                            int64_t row_bytes, int32_t* err_word, void* stream) {
+  if (n_tensors < 1 || n_tensors > 3)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "n_tensors must be 1, 2 or 3");
+  if (src == nullptr || dst == nullptr || src_rows == nullptr || dst_rows == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  for (int t = 0; t < n_tensors; ++t)
+    if (src[t] == nullptr || dst[t] == nullptr)
+      return fail(BSA_ERR_INVALID_ARGUMENT, "null tensor pointer %d", t);
+  if (batch < 0 || rows < 0 || tokens_in < 0 || tokens_dst < 0 || row_bytes <= 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "negative size or empty row");
+  cudaError_t e = bsa::launch_reorder_rows(n_tensors, src, dst, src_rows, batch, rows, tokens_in,
+                                           row_bytes, err_word, static_cast<cudaStream_t>(stream),
+                                           sm_count(), dst_rows, tokens_dst);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_gather_scatter_rows launch");
+  return ok();
+}
+
 int bsa_pack_boolean_rows(const uint8_t* route, int64_t rows, int32_t cols, int32_t* counts,
                           int32_t* indices, void* stream) {
   if (route == nullptr || counts == nullptr || indices == nullptr)

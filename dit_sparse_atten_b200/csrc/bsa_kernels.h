@@ -11,10 +11,12 @@
 namespace bsa {
 
 // ---- (c) reorder ----------------------------------------------------------
+// dst_rows (optional): destination row of output index i, in [0, tokens_dst).
 cudaError_t launch_reorder_rows(int n_tensors, const void* const* src, void* const* dst,
                                 const int32_t* perm, int64_t batch, int64_t tokens_out,
                                 int64_t tokens_in, int64_t row_bytes, int* err_word,
-                                cudaStream_t stream, int num_sms);
+                                cudaStream_t stream, int num_sms,
+                                const int32_t* dst_rows = nullptr, int64_t tokens_dst = 0);
 
 // ---- (b) route selection / CSR pack ----------------------------------------
 struct SelectArgs {

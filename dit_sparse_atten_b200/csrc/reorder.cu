@@ -1,7 +1,9 @@
 // (c) Spatial reorder: out[t][b][i][:] = src[t][b][perm[i]][:] for up to three
 // tensors sharing one permutation.  Pack (Q/K/V into Morton order) and unpack
 // (output back to raster order, with the inverse permutation) are both this
-// gather, so every store is a coalesced full row.
+// gather, so every store is a coalesced full row.  With a destination row map
+// the same kernel writes out[t][b][dst_rows[i]] instead (the head-parallel
+// exchange uses it to lay rows out for the all-to-all).
 //
 // Reference semantics: attention_backends/spatial.py:82-93 (index_select on
 // axis 1) and the fused Triton gather attention_backends/layout_ops.py:21-52,
@@ -18,9 +20,11 @@ struct ReorderArgs {
   const uint8_t* src[3];
   uint8_t* dst[3];
   const int32_t* perm;
+  const int32_t* dst_rows;  // destination row of each output index, or null (row i)
   int64_t batch;
-  int64_t tokens_out;
+  int64_t tokens_out;       // output indices per batch element
   int64_t tokens_in;
+  int64_t tokens_dst;       // destination rows per batch element
   int64_t row_bytes;
   int64_t rows_per_tensor;  // batch * tokens_out
   int n_tensors;
@@ -47,10 +51,18 @@ __global__ void __launch_bounds__(kReorderWarps * 32)
       if (lane == 0 && a.err_word) atomicOr(a.err_word, kErrBadRoute);
       continue;
     }
+    int64_t d = i;
+    if (a.dst_rows != nullptr) {
+      d = __ldg(a.dst_rows + i);
+      if (d < 0 || d >= a.tokens_dst) {
+        if (lane == 0 && a.err_word) atomicOr(a.err_word, kErrBadRoute);
+        continue;
+      }
+    }
     const uint8_t* src_base = t == 0 ? a.src[0] : (t == 1 ? a.src[1] : a.src[2]);
     uint8_t* dst_base = t == 0 ? a.dst[0] : (t == 1 ? a.dst[1] : a.dst[2]);
     const Vec* src = reinterpret_cast<const Vec*>(src_base + (b * a.tokens_in + s) * a.row_bytes);
-    Vec* dst = reinterpret_cast<Vec*>(dst_base + (b * a.tokens_out + i) * a.row_bytes);
+    Vec* dst = reinterpret_cast<Vec*>(dst_base + (b * a.tokens_dst + d) * a.row_bytes);
     int64_t v = lane;
     for (; v + 32 * (kUnroll - 1) < nvec; v += 32 * kUnroll) {
       Vec tmp[kUnroll];
@@ -68,8 +80,11 @@ __global__ void __launch_bounds__(kReorderWarps * 32)
 cudaError_t launch_reorder_rows(int n_tensors, const void* const* src, void* const* dst,
                                 const int32_t* perm, int64_t batch, int64_t tokens_out,
                                 int64_t tokens_in, int64_t row_bytes, int* err_word,
-                                cudaStream_t stream, int num_sms) {
+                                cudaStream_t stream, int num_sms, const int32_t* dst_rows,
+                                int64_t tokens_dst) {
   ReorderArgs a{};
+  a.dst_rows = dst_rows;
+  a.tokens_dst = dst_rows != nullptr ? tokens_dst : tokens_out;
   uintptr_t align_bits = static_cast<uintptr_t>(row_bytes);
   for (int t = 0; t < n_tensors; ++t) {
     a.src[t] = static_cast<const uint8_t*>(src[t]);

@@ -76,6 +76,49 @@ def reorder_rows(tensors: Sequence[torch.Tensor], perm: torch.Tensor,
     return tuple(outs)
 
 
+def gather_scatter_rows(srcs: Sequence[torch.Tensor], dsts: Sequence[torch.Tensor],
+                        src_rows: torch.Tensor, dst_rows: torch.Tensor,
+                        dst_offsets: Sequence[int] | None = None) -> None:
+    """``dst[t][b, off_t + dst_rows[i]] = src[t][b, src_rows[i]]`` for 1-3 pairs
+    of ``[B, tokens, ...]`` tensors with equal row sizes
+    (``bsa_gather_scatter_rows``): the row moves of the head-parallel exchange.
+    ``dsts`` are written in place and must be contiguous; ``dst_offsets``
+    (rows, default 0) lets several sources land in one destination buffer."""
+    if not 1 <= len(srcs) == len(dsts) <= 3:
+        raise ValueError("one to three source/destination pairs")
+    offsets = list(dst_offsets) if dst_offsets is not None else [0] * len(dsts)
+    if len(offsets) != len(dsts) or any(o < 0 for o in offsets):
+        raise ValueError("one non-negative row offset per destination")
+    device = _require_cuda(*srcs, *dsts, src_rows, dst_rows)
+    first, out0 = srcs[0], dsts[0]
+    if any(t.shape[0] != first.shape[0] for t in (*srcs, *dsts)):
+        raise ValueError("sources and destinations must share the batch size")
+    row_bytes = first[0, 0].numel() * first.element_size()
+    if any(t[0, 0].numel() * t.element_size() != row_bytes for t in (*srcs, *dsts)):
+        raise ValueError("sources and destinations must share the row size")
+    if any(not t.is_contiguous() for t in (*srcs, *dsts)):
+        raise ValueError("gather_scatter_rows needs contiguous tensors")
+    src_rows = src_rows.to(device=device, dtype=torch.int32).contiguous()
+    dst_rows = dst_rows.to(device=device, dtype=torch.int32).contiguous()
+    if src_rows.numel() != dst_rows.numel():
+        raise ValueError("src_rows and dst_rows must have equal lengths")
+    n = len(srcs)
+    if src_rows.numel() == 0 or first.shape[0] == 0:
+        return
+    if any(o > t.shape[1] for o, t in zip(offsets, dsts)):
+        raise ValueError("row offset past the destination")
+    if any(offsets) and first.shape[0] != 1:
+        raise ValueError("row offsets need batch 1")
+    # rows addressable from every destination's offset base
+    tokens_dst = min(t.shape[1] - o for o, t in zip(offsets, dsts))
+    src = (ctypes.c_void_p * 3)(*([t.data_ptr() for t in srcs] + [0] * (3 - n)))
+    dst = (ctypes.c_void_p * 3)(*([t.data_ptr() + o * row_bytes for o, t in zip(offsets, dsts)]
+                                  + [0] * (3 - n)))
+    _native.call("bsa_gather_scatter_rows", n, src, dst, src_rows.data_ptr(), dst_rows.data_ptr(),
+                 first.shape[0], src_rows.numel(), first.shape[1], tokens_dst, row_bytes,
+                 _native.err_word(device).data_ptr(), _stream(device))
+
+
 # ----------------------------------------------------------------------------
 # (b) route: sampling, mass, selection, CSR
 # ----------------------------------------------------------------------------

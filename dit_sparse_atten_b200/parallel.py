@@ -99,26 +99,105 @@ def head_to_seq(x, group, group_size):
     return recv.permute(1, 2, 0, 3, 4).reshape(b, t_local, group_size * hp, d)
 
 
-def head_parallel_attention(q, k, v, attend, group, group_size):
+class CudaRows:
+    """Row moves of the exchange on the GPU: ``gather`` is ``kernels.reorder_rows``
+    (``out[b, i] = x[b, perm[i]]``), ``scatter`` is
+    ``kernels.gather_scatter_rows`` (``dst[b, off + dst_rows[i]] = src[b, src_rows[i]]``)."""
+
+    @staticmethod
+    def gather(tensors, perm):
+        from . import kernels
+        return kernels.reorder_rows(tensors, perm)
+
+    @staticmethod
+    def scatter(srcs, dsts, src_rows, dst_rows, dst_offsets=None):
+        from . import kernels
+        kernels.gather_scatter_rows(srcs, dsts, src_rows, dst_rows, dst_offsets)
+
+
+class _Tables:
+    """Row maps of one exchange shape, built once on the CPU, cached per device."""
+
+    def __init__(self, builders):
+        self._builders = builders
+        self._cpu = {name: fn().to(torch.int32) for name, fn in builders.items()}
+        self._dev = {}
+
+    def get(self, name, device):
+        key = (name, device)
+        if key not in self._dev:
+            self._dev[key] = self._cpu[name].to(device)
+        return self._dev[key]
+
+
+def _send_maps(P, tl, groups):
+    """For a sequence shard ``[tl, P * groups, rowsz]`` (rows of one head
+    group): the source row and send-buffer row of every (destination rank p,
+    token i) for head group ``g`` of each rank, the send buffer being
+    ``[P, 3, tl, rowsz]`` with Q, K, V at row offsets 0, tl, 2 tl."""
+    p = torch.arange(P)[:, None]
+    i = torch.arange(tl)[None, :]
+    dst = (p * 3 * tl + i).reshape(-1)
+
+    def src(g):
+        return ((i * P + p) * groups + g).reshape(-1)
+    return src, dst
+
+
+def head_parallel_attention(q, k, v, attend, group, group_size, rows=None):
     """Run ``attend(q, k, v) -> out`` on head shards of sequence-sharded inputs.
 
     ``q, k, v``: ``[B, T/P, H, D]``; ``attend`` receives ``[B, T, H/P, D]``
     tensors and returns the same shape (for example pack -> block-sparse
-    attention over this rank's heads' CSR routes -> unpack).
+    attention over this rank's heads' CSR routes -> unpack).  With batch 1 the
+    send buffer is written by one row gather (no concatenation or transpose
+    copies), the received rows are gathered into token order, and the output
+    rows are scattered back into ``[T/P, H, D]``; ``rows`` supplies those row
+    moves (``CudaRows`` by default).
     """
-    stacked = torch.cat([q, k, v], 0)             # one exchange for Q, K and V
-    heads = seq_to_head(stacked, group, group_size)
-    b = q.shape[0]
-    out = attend(heads[:b], heads[b:2 * b], heads[2 * b:])
-    return head_to_seq(out, group, group_size)
+    if group_size == 1:
+        return attend(q, k, v)
+    b, tl, h, d = q.shape
+    if b != 1:
+        stacked = torch.cat([q, k, v], 0)             # one exchange for Q, K and V
+        heads = seq_to_head(stacked, group, group_size)
+        out = attend(heads[:b], heads[b:2 * b], heads[2 * b:])
+        return head_to_seq(out, group, group_size)
+    rows = rows or CudaRows
+    P = group_size
+    hp = h // P
+    T = P * tl
+    src_of, dst = _send_maps(P, tl, 1)
+    src = src_of(0)
+    send = torch.empty((P * 3 * tl, hp, d), dtype=q.dtype, device=q.device)
+    flat = [x.contiguous().view(1, tl * P, hp, d) for x in (q, k, v)]
+    rows.scatter(flat, [send[None]] * 3, src.to(q.device, torch.int32),
+                 dst.to(q.device, torch.int32), dst_offsets=[0, tl, 2 * tl])
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    # recv = [src rank p, q|k|v, tl, hp, d]: token p * tl + i of tensor t is
+    # row (p * 3 + t) * tl + i
+    g = torch.arange(T)
+    order = ((g // tl) * 3 * tl + g % tl).to(q.device, torch.int32)
+    span = (3 * P - 2) * tl
+    r = recv[None]
+    qh, kh, vh = rows.gather([r[:, t * tl:t * tl + span] for t in range(3)], order)
+    out_h = attend(qh, kh, vh).contiguous()
+    orecv = torch.empty_like(out_h)
+    dist.all_to_all_single(orecv, out_h, group=group)
+    # orecv = [src rank p, tl, hp, d] -> out [tl, P, hp, d]: row p*tl + i -> i*P + p
+    out = torch.empty_like(q)
+    rows.scatter([orecv.view(1, T, hp, d)], [out.view(1, T, hp, d)],
+                 torch.arange(T, dtype=torch.int32, device=q.device), src.to(q.device, torch.int32))
+    return out
 
 
 def pipeline_chunks(heads_per_rank):
-    """Head chunks per rank for ``PipelinedHeadParallel``: 4, 2, 5 or 3 chunks
-    of at least 4 heads each (enough attention per chunk to hide the next
-    chunk's exchange), else 1."""
-    for c in (4, 2, 5, 3):
-        if heads_per_rank % c == 0 and heads_per_rank // c >= 4:
+    """Head chunks per rank for ``PipelinedHeadParallel``: the most chunks (up
+    to 5) of at least 2 heads each, so the exposed first input exchange and
+    last output exchange are a small share of the step."""
+    for c in (5, 4, 3, 2):
+        if heads_per_rank % c == 0 and heads_per_rank // c >= 2:
             return c
     return 1
 
@@ -127,24 +206,25 @@ class PipelinedHeadParallel:
     """Ulysses exchange in head chunks, overlapped with the attention.
 
     For one CFG branch (batch 1) of sequence shards ``[1, T/P, H, D]``: this
-    rank's ``H/P`` heads are split into ``chunks`` groups.  The input
-    all-to-all of every chunk is issued up front on NCCL's stream; chunk c's
-    packed Q/K/V are gathered straight from its receive buffer (no
-    concatenation or transpose copies: the pack permutation is remapped onto
-    the receive layout ``[src rank, q|k|v, T/P, heads, D]``), ``attend`` runs
-    on them, the result is restored to token order - which is already the
-    send layout of the output all-to-all - and sent back while the next chunk
-    computes.  Only the first chunk's input exchange and the last chunk's
-    output exchange stay exposed.
+    rank's ``H/P`` heads are split into ``chunks`` groups.  Every chunk's send
+    buffer ``[P, q|k|v, T/P, hc, D]`` is written by one row-gather launch and
+    its input all-to-all issued up front on NCCL's stream.  Chunk c's packed
+    Q/K/V are gathered straight from its receive buffer (the pack permutation
+    remapped onto the receive layout), ``attend`` runs on them and stores its
+    output rows in token order - the send layout of the output all-to-all -
+    which is sent while the next chunk computes; each received output chunk
+    is scattered into ``[T/P, H, D]`` by one launch.  Only the first chunk's
+    input exchange and the last chunk's output exchange stay exposed.
 
-    ``attend(qp, kp, vp, chunk) -> out_p`` takes and returns ``[1, T, hc, D]``
-    tensors in pack order (for example the routed attention over the chunk's
-    heads' CSR).  ``gather(tensors, perm)`` is the row gather
-    (``kernels.reorder_rows`` on GPUs; CPU tests pass an ``index_select``).
+    ``attend(qp, kp, vp, chunk, out, out_rows)`` gets ``[1, T, hc, D]`` tensors
+    in pack order and either writes the output to token ``out_rows[i]`` of
+    ``out`` (``[1, T, hc, D]``; ``out_rows`` is None without a permutation) and
+    returns None - the block-sparse kernel's folded unpack - or returns the
+    output in pack order.  ``rows`` supplies the row moves (``CudaRows``).
     """
 
     def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
-                 chunks=None, gather=None):
+                 chunks=None, rows=None):
         if heads % group_size:
             raise ValueError(f"{heads} heads do not split over {group_size} ranks")
         self.group = group
@@ -162,55 +242,63 @@ class PipelinedHeadParallel:
                 else torch.as_tensor(perm).to("cpu", torch.int64))
         if perm.numel() != tokens:
             raise ValueError("perm must cover the whole sequence")
-        src, local = perm // tokens_local, perm % tokens_local
-        # row of token perm[i] of tensor 0 in the receive buffer viewed as
-        # [P * 3 * T/P] rows; tensor t starts t * T/P rows later
-        self._src_perm = (src * 3 * tokens_local + local).to(torch.int32)
-        self._inverse = None if inverse is None else torch.as_tensor(inverse).to(torch.int32)
-        self._dev = {}
-        if gather is None:
-            from . import kernels
-            gather = kernels.reorder_rows
-        self.gather = gather
-
-    def _device_tables(self, device):
-        if device not in self._dev:
-            self._dev[device] = (self._src_perm.to(device),
-                                 None if self._inverse is None else self._inverse.to(device))
-        return self._dev[device]
+        self.has_perm = inverse is not None
+        P, tl, C = self.P, self.tl, self.chunks
+        src_of, dst = _send_maps(P, tl, C)
+        src, local = perm // tl, perm % tl
+        builders = {"recv_perm": lambda: src * 3 * tl + local,   # row of token perm[i], tensor 0
+                    "send_dst": lambda: dst,
+                    "out_src": lambda: torch.arange(P * tl),
+                    "perm": lambda: perm}
+        for c in range(C):
+            builders[f"send_src{c}"] = (lambda c=c: src_of(c))
+        if inverse is not None:
+            inv = torch.as_tensor(inverse).to("cpu", torch.int64)
+            builders["inverse"] = lambda: inv
+        self.tables = _Tables(builders)
+        self.rows = rows or CudaRows
 
     def __call__(self, q, k, v, attend):
         b, tl, h, d = q.shape
         if b != 1 or tl != self.tl or h != self.hp * self.P:
             raise ValueError("PipelinedHeadParallel takes [1, T/P, H, D] shards of one branch")
-        P, hp, hc, C = self.P, self.hp, self.hc, self.chunks
-        src_perm, inverse = self._device_tables(q.device)
-        send = torch.empty((C, P, 3, tl, hc, d), dtype=q.dtype, device=q.device)
+        P, hc, C = self.P, self.hc, self.chunks
+        T = P * tl
+        dev = q.device
+        tab = lambda name: self.tables.get(name, dev)  # noqa: E731
+        flat = [x.contiguous().view(1, tl * P * C, hc, d) for x in (q, k, v)]
+        send = torch.empty((C, P * 3 * tl, hc, d), dtype=q.dtype, device=dev)
         recv = torch.empty_like(send)
         inputs = []
         for c in range(C):
-            for t, x in enumerate((q, k, v)):
-                send[c, :, t].copy_(x[0].view(tl, P, hp, d)[:, :, c * hc:(c + 1) * hc]
-                                    .permute(1, 0, 2, 3))
+            self.rows.scatter(flat, [send[c][None]] * 3, tab(f"send_src{c}"), tab("send_dst"),
+                              dst_offsets=[0, tl, 2 * tl])
             inputs.append(dist.all_to_all_single(recv[c], send[c], group=self.group,
                                                  async_op=True))
         span = (3 * P - 2) * tl
-        outputs, sent = [], []
-        orecv = torch.empty((C, P, tl, hc, d), dtype=q.dtype, device=q.device)
+        out_send = torch.empty((C, T, hc, d), dtype=q.dtype, device=dev)
+        orecv = torch.empty_like(out_send)
+        outputs = []
+        out_rows = tab("perm") if self.has_perm else None
         for c in range(C):
             inputs[c].wait()
-            flat = recv[c].view(1, P * 3 * tl, hc, d)
-            qp, kp, vp = self.gather([flat[:, t * tl:t * tl + span] for t in range(3)], src_perm)
-            out_p = attend(qp, kp, vp, c)
-            out_c = out_p if inverse is None else self.gather([out_p], inverse)[0]
-            sent.append(out_c)
-            outputs.append(dist.all_to_all_single(orecv[c], out_c.view(P, tl, hc, d),
-                                                  group=self.group, async_op=True))
+            r = recv[c][None]
+            qp, kp, vp = self.rows.gather([r[:, t * tl:t * tl + span] for t in range(3)],
+                                          tab("recv_perm"))
+            res = attend(qp, kp, vp, c, out_send[c][None], out_rows)
+            if res is not None:          # output in pack order: unpack it here
+                if self.has_perm:
+                    self.rows.scatter([res.contiguous()], [out_send[c][None]], tab("out_src"),
+                                      tab("perm"))
+                else:
+                    out_send[c].copy_(res[0])
+            outputs.append(dist.all_to_all_single(orecv[c], out_send[c], group=self.group,
+                                                  async_op=True))
         out = torch.empty_like(q)
+        dst = out.view(1, tl * P * C, hc, d)
         for c in range(C):
             outputs[c].wait()
-            out[0].view(tl, P, hp, d)[:, :, c * hc:(c + 1) * hc].copy_(
-                orecv[c].permute(1, 0, 2, 3))
+            self.rows.scatter([orecv[c][None]], [dst], tab("out_src"), tab(f"send_src{c}"))
         return out
 
 

@@ -66,6 +66,24 @@ BSA_API int bsa_reorder_rows(int32_t n_tensors, const void* const* src, void* co
                      int64_t row_bytes, int32_t* err_word, void* stream);
 
 /*
+ * (e) Row gather with a destination map, for the head-parallel (Ulysses)
+ * exchange: for t < n_tensors, b < batch, i < rows:
+ *   dst[t][b, dst_rows[i], :] = src[t][b, src_rows[i], :]
+ * with `row_bytes`-byte rows, [batch, tokens_in, row] sources and
+ * [batch, tokens_dst, row] destinations.  Out-of-range entries of either map
+ * are skipped and flag BSA_DEVICE_BAD_ROUTE.  It lays Q/K/V head chunks out
+ * as the all-to-all's send buffer and scatters received output chunks back
+ * into [tokens, heads, D] without strided copies.
+ * Replaces: nothing in the reference, which runs on one device; the
+ * exchange is this build's multi-GPU layer.
+ */
+BSA_API int bsa_gather_scatter_rows(int32_t n_tensors, const void* const* src, void* const* dst,
+                                    const int32_t* src_rows, const int32_t* dst_rows,
+                                    int64_t batch, int64_t rows, int64_t tokens_in,
+                                    int64_t tokens_dst, int64_t row_bytes, int32_t* err_word,
+                                    void* stream);
+
+/*
  * CSR pack of a boolean route [rows, cols] (uint8 0/1): counts[r] = number of
  * selected columns; indices[r, :] = selected column ids ascending, then the
  * unselected ids ascending.  cols <= 4096.

@@ -1,0 +1,104 @@
+"""Head-parallel exchange on real GPUs (NCCL), when the box has two or more.
+
+Two ranks hold sequence shards of one branch; both exchange paths - the
+unchunked ``head_parallel_attention`` (the backend API's path) and the
+chunked ``PipelinedHeadParallel`` with the routed kernel storing into the
+output all-to-all's send buffer - must give the single-GPU result on every
+row of the rank's shard.  Skipped with fewer than two GPUs; the host-side
+layout logic is covered on CPU by tests/test_parallel_gloo.py.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from dit_sparse_atten_b200 import _native, kernels, parallel
+    from dit_sparse_atten_b200.spatial import build_spatial_layout
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        grid, H = (4, 16, 32), 8                  # 2,048 tokens, 16 route blocks
+        T = grid[0] * grid[1] * grid[2]
+        g = torch.Generator().manual_seed(0)
+        q, k, v = (torch.randn((1, T, H, 128), generator=g).to(torch.bfloat16).to(dev)
+                   for _ in range(3))
+        route = torch.rand((H, 16, 16), generator=g) < 0.5
+        route[..., 0] = True
+        lay = build_spatial_layout(grid, 128)
+        counts, indices = kernels.pack_boolean_rows(route.to(dev))
+        # single-GPU reference: pack, routed attention, unpack
+        qp, kp, vp = lay.reorder_qkv(q, k, v)
+        ref = lay.restore(kernels.block_sparse_attention(qp, kp, vp, counts, indices))
+        tl = T // world
+        sl = slice(rank * tl, (rank + 1) * tl)
+        hp = H // world
+        hs = slice(rank * hp, (rank + 1) * hp)
+        c_loc, i_loc = counts[hs].contiguous(), indices[hs].contiguous()
+
+        def attend(qh, kh, vh):
+            a, b_, c = lay.reorder_qkv(qh, kh, vh)
+            return kernels.block_sparse_attention(a, b_, c, c_loc, i_loc,
+                                                  out_rows=lay.permutation(dev))
+
+        out = parallel.head_parallel_attention(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                               v[:, sl].contiguous(), attend,
+                                               dist.group.WORLD, world)
+        errs = [float((out.float() - ref[:, sl].float()).abs().max())]
+        pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
+                                              perm=lay.permutation_cpu, inverse=lay.inverse_cpu,
+                                              chunks=2)
+        hc = pipe.hc
+
+        def attend_chunk(qp_, kp_, vp_, c, out_c, out_rows):
+            cs = slice(c * hc, (c + 1) * hc)
+            kernels.block_sparse_attention(qp_, kp_, vp_, c_loc[cs].contiguous(),
+                                           i_loc[cs].contiguous(), out=out_c, out_rows=out_rows)
+
+        out2 = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
+                    attend_chunk)
+        torch.cuda.synchronize()
+        _native.check_device_errors()
+        errs.append(float((out2.float() - ref[:, sl].float()).abs().max()))
+        queue.put((rank, errs))
+    except Exception as exc:
+        queue.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_exchange_paths_match_single_gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in results.items():
+        assert not isinstance(errs, str), errs
+        # the same kernels on the same rows: the exchange must not change a bit
+        assert errs == [0.0, 0.0], (rank, errs)

@@ -372,3 +372,27 @@ def test_dense_attention_block_mass(B, T, H, workspace):
     for b in range(B):
         ref, _ = _exact_reference(q[b:b + 1].cpu(), k[b:b + 1].cpu(), 128)
         np.testing.assert_allclose(mass[b].cpu().numpy(), ref, atol=2e-3, rtol=1e-3)
+
+
+def test_gather_scatter_rows_with_offsets():
+    """bsa_gather_scatter_rows: src/dst row maps, three tensors into one
+    buffer at row offsets, out-of-range map entries skipped and reported."""
+    g = torch.Generator().manual_seed(4)
+    src = [torch.randn((1, 50, 2, 8), generator=g).to(DEV) for _ in range(3)]
+    src_rows = torch.randint(0, 50, (30,), generator=g, dtype=torch.int32)
+    dst_rows = torch.randperm(40, generator=g)[:30].to(torch.int32)
+    buf = torch.zeros((1, 120, 2, 8), device=DEV)
+    kernels.gather_scatter_rows(src, [buf] * 3, src_rows.to(DEV), dst_rows.to(DEV),
+                                dst_offsets=[0, 40, 80])
+    torch.cuda.synchronize()
+    _native.check_device_errors()
+    expect = torch.zeros_like(buf)
+    for t in range(3):
+        expect[0, 40 * t + dst_rows.long()] = src[t][0, src_rows.long()]
+    assert torch.equal(buf, expect)
+    bad = dst_rows.clone()
+    bad[3] = 500
+    kernels.gather_scatter_rows(src[:1], [buf], src_rows.to(DEV), bad.to(DEV))
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="out of range"):
+        _native.check_device_errors()

@@ -61,6 +61,21 @@ def _exchange(rank, world):
     return True
 
 
+class CpuRows:
+    """The exchange's row moves with torch indexing (the product uses the
+    CUDA row-gather kernels): the host-side layout logic under test."""
+
+    @staticmethod
+    def gather(tensors, perm):
+        return tuple(t.index_select(1, perm.long()) for t in tensors)
+
+    @staticmethod
+    def scatter(srcs, dsts, src_rows, dst_rows, dst_offsets=None):
+        offsets = dst_offsets or [0] * len(dsts)
+        for src, dst, off in zip(srcs, dsts, offsets):
+            dst[:, off + dst_rows.long()] = src[:, src_rows.long()]
+
+
 def _attention(rank, world):
     q, k, v = full_inputs()
     t = q.shape[1] // world
@@ -71,14 +86,15 @@ def _attention(rank, world):
             qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2)).transpose(1, 2)
 
     out = parallel.head_parallel_attention(q[:, sl], k[:, sl], v[:, sl], attend,
-                                           dist.group.WORLD, world)
+                                           dist.group.WORLD, world, rows=CpuRows)
     ref = attend(q, k, v)[:, sl]
     torch.testing.assert_close(out, ref)
+    # batch 2 takes the generic (concatenating) exchange
+    q2, k2, v2 = (torch.cat([x, x.flip(1)], 0) for x in (q, k, v))
+    out2 = parallel.head_parallel_attention(q2[:, sl], k2[:, sl], v2[:, sl], attend,
+                                            dist.group.WORLD, world)
+    torch.testing.assert_close(out2, attend(q2, k2, v2)[:, sl])
     return True
-
-
-def _cpu_gather(tensors, perm):
-    return tuple(t.index_select(1, perm.long()) for t in tensors)
 
 
 def _pipelined(rank, world):
@@ -94,26 +110,35 @@ def _pipelined(rank, world):
         return torch.nn.functional.scaled_dot_product_attention(
             qh.transpose(1, 2), kh.transpose(1, 2), vh.transpose(1, 2)).transpose(1, 2)
 
-    def attend(qp, kp, vp, chunk):
+    def attend(qp, kp, vp, chunk, out, out_rows):
         seen.append(chunk)
         return sdpa(qp, kp, vp)         # permutation-equivariant: output stays in pack order
 
+    def attend_scatter(qp, kp, vp, chunk, out, out_rows):
+        # the folded unpack: write row i to token out_rows[i]
+        res = sdpa(qp, kp, vp)
+        rows = torch.arange(res.shape[1]) if out_rows is None else out_rows.long()
+        out[:, rows] = res
+        return None
+
     ref = sdpa(q, k, v)[:, sl]
     for kw in ({"perm": perm, "inverse": inverse, "chunks": 2}, {"chunks": 1}, {"chunks": 2}):
-        seen.clear()
-        pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, q.shape[2], t,
-                                              gather=_cpu_gather, **kw)
-        out = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), attend)
-        torch.testing.assert_close(out, ref)
-        assert seen == list(range(kw["chunks"]))
+        for fn in (attend, attend_scatter):
+            seen.clear()
+            pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, q.shape[2], t,
+                                                  rows=CpuRows, **kw)
+            out = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), fn)
+            torch.testing.assert_close(out, ref)
+            if fn is attend:
+                assert seen == list(range(kw["chunks"]))
     # the packed inputs of a chunk are exactly this rank's heads in pack order
     got = {}
 
-    def capture(qp, kp, vp, chunk):
+    def capture(qp, kp, vp, chunk, out, out_rows):
         got[chunk] = qp.clone()
         return qp
     pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, q.shape[2], t, perm=perm,
-                                          inverse=inverse, chunks=2, gather=_cpu_gather)
+                                          inverse=inverse, chunks=2, rows=CpuRows)
     pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), capture)
     hp = q.shape[2] // world
     for c in range(2):
@@ -142,7 +167,7 @@ def test_pipelined_exchange_equals_full_attention():
 
 
 def test_pipeline_chunk_rule():
-    assert [parallel.pipeline_chunks(h) for h in (40, 20, 10, 5, 8, 12)] == [4, 4, 2, 1, 2, 2]
+    assert [parallel.pipeline_chunks(h) for h in (40, 20, 10, 5, 8, 12, 3)] == [5, 5, 5, 1, 4, 4, 1]
     with pytest.raises(ValueError):
         parallel.PipelinedHeadParallel(None, 2, 40, 16, chunks=3)
     with pytest.raises(ValueError):

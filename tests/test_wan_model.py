@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 
 from dit_sparse_atten_b200 import parallel, wan_model
-from test_parallel_gloo import run_ranks
+from test_parallel_gloo import CpuRows, run_ranks
 
 TINY = wan_model.WanConfig(dim=64, ffn=96, heads=4, layers=2, in_channels=4, out_channels=4,
                            text_dim=24, text_tokens=8, freq_dim=16)
@@ -67,7 +67,8 @@ def generate(branches, shard, combine):
     contexts = {b: model.context(text[b]) for b in branches}
 
     def attention(q, k, v):
-        return parallel.head_parallel_attention(q, k, v, sdpa, shard.group, shard.size)
+        return parallel.head_parallel_attention(q, k, v, sdpa, shard.group, shard.size,
+                                                rows=CpuRows)
 
     return wan_model.denoise(model, rows, contexts, attention, combine, steps=STEPS)
 
