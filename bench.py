@@ -880,7 +880,8 @@ def gpu_comparator(cfg, q, k, v, qp, kp, vp, route_all, counts, indices, stages,
             times.append(e0.elapsed_time(e1))
         return statistics.median(times)
 
-    res = {"reference": f"{ref.root}: the reference's attention_backends, unmodified "
+    where = os.path.relpath(ref.root, REPO) if ref.root.startswith(str(REPO)) else "$BSA_REFERENCE"
+    res = {"reference": f"{where}: the reference's attention_backends, unmodified "
                         f"(torch {torch.__version__}, FlexAttention compiled by Inductor)",
            "errors": {}}
     t0 = time.perf_counter()

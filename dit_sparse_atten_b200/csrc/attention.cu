@@ -52,11 +52,27 @@ namespace {
 
 using namespace attn;
 
-constexpr int kSoftmaxWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;      // S issuer, TMEM owner
-constexpr int kPvWarp = 10;      // PV issuer
-constexpr int kAttnThreads = 352;
+// Softmax groups of four warps; group g takes the key blocks j with
+// j % kGroups == g.  Three groups run with a register split (setmaxnreg):
+// 512 threads launched with kLaunchRegs each, the control warpgroup (TMA
+// producer, the two MMA issuers, one idle warp) gives registers back and the
+// three softmax warpgroups take them.
+#ifndef BSA_SOFTMAX_GROUPS
+#define BSA_SOFTMAX_GROUPS 2
+#endif
+constexpr int kGroups = BSA_SOFTMAX_GROUPS;
+static_assert(kGroups == 2 || kGroups == 3, "two or three softmax groups");
+constexpr int kSoftmaxWarps = 4 * kGroups;
+constexpr int kProducerWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;   // S issuer, TMEM owner
+constexpr int kPvWarp = kSoftmaxWarps + 2;    // PV issuer
+constexpr int kAttnThreads = kGroups == 2 ? 352 : 512;
+constexpr bool kRegSplit = kGroups == 3;
+constexpr uint32_t kLaunchRegs = 128;         // 512 threads x 128 = 65,536
+constexpr uint32_t kSoftRegs = 144;
+constexpr uint32_t kCtrlRegs = 64;
+static_assert(!kRegSplit || 3 * 128 * kSoftRegs + 128 * kCtrlRegs <= kAttnThreads * kLaunchRegs,
+              "register split must stay within the launch total");
 constexpr int kHeadDim = 128;
 constexpr int kSBuffers = 3;            // S/P buffers in TMEM
 constexpr uint32_t kTmemO = 384;
@@ -68,16 +84,22 @@ constexpr uint32_t kTmemO = 384;
 #define BSA_EMULATED_PAIRS 0
 #endif
 constexpr int kEmulatedPairsPer8 = BSA_EMULATED_PAIRS;
+// S-row chunks kept in registers between the max and exponential passes.
+#ifndef BSA_KEPT_CHUNKS
+#define BSA_KEPT_CHUNKS 0
+#endif
+template <int BK>
+constexpr int kKeep = BSA_KEPT_CHUNKS > 0 && BK == 128 ? BSA_KEPT_CHUNKS : kKeptChunks<BK>;
 
 template <int BK>
 struct AttnLayout {
   static constexpr int kSlotPanel = BK * 128;            // one 64-column panel of K or V
   static constexpr int kSlotBytes = 2 * kSlotPanel;
-  static constexpr int kSlots = BK == 128 ? 6 : 12;
+  static constexpr int kSlots = BK == 128 ? (kGroups == 2 ? 6 : 5) : 12;
   static constexpr int kQOff = 0;                                // Q tile, 128 rows x 256 B
   static constexpr int kRingOff = kQOff + 128 * 256;
   static constexpr int kXOff = kRingOff + kSlots * kSlotBytes;   // stabiliser hand-over
-  static constexpr int kXBytes = 2 * 2 * 128 * 4;                // [2][2][row] floats
+  static constexpr int kXBytes = 2 * kGroups * 128 * 4;          // [2][groups][row] floats
   static constexpr int kBarOff = kXOff + kXBytes;
   static constexpr int kBarBytes = 320;
   static constexpr int kUsed = kBarOff + kBarBytes;
@@ -148,11 +170,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(&bar->q_full, 1);
     for (int i = 0; i < kSBuffers; ++i) {
       mbar_init(&bar->s_full[i], 1);
-      mbar_init(&bar->p_full[i], kSoftmaxWarps * 16);   // one group per block
+      mbar_init(&bar->p_full[i], 128);   // one group (128 threads) per block
       mbar_init(&bar->o_done[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar->m_full[i], kSoftmaxWarps * 16);
+      mbar_init(&bar->m_full[i], 128);
       mbar_init(&bar->drain[i], 1);
     }
     for (int s = 0; s < L::kSlots; ++s) {
@@ -181,7 +203,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     return kb;
   };
 
-  if (warp == kProducerWarp) {
+  if (warp >= kSoftmaxWarps) {
+   if constexpr (kRegSplit) setmaxnreg_dec<kCtrlRegs>();
+   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm_k);
@@ -215,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int s = 0; s < L::kSlots; ++s)
         if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
-  } else if (warp == kMmaWarp || warp == kPvWarp) {
+   } else if (warp == kMmaWarp || warp == kPvWarp) {
     // ------------------------------------------------------------ MMA issuers
     // Load sequence of the producer: K0, then K_{j+1}, V_j for every j.
     auto seq_k = [](int j) { return j == 0 ? 0 : 2 * j - 1; };
@@ -281,18 +305,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       umma_commit(&bar->drain[1]);
       mbar_wait(&bar->drain[1], 0, &never, a.err_word);
     }
+   }
   } else {
+    if constexpr (kRegSplit) setmaxnreg_inc<kSoftRegs>();
     // ------------------------------------------------------------ softmax
-    // Two groups of four warps take alternate key blocks: group g = warp / 4
-    // handles blocks j with j % 2 == g, one full row per thread (warp w owns
-    // TMEM lanes 32*(w%4)..), so each group has two block periods for its
-    // softmax.  The stabiliser moves from group to group through m_buf and the
-    // m_full barriers; each group keeps its own row sum.
+    // kGroups groups of four warps take turns over the key blocks: group
+    // g = warp / 4 handles blocks j with j % kGroups == g, one full row per
+    // thread (warp w owns TMEM lanes 32*(w%4)..), so each group has kGroups
+    // block periods for its softmax.  The stabiliser moves from group to
+    // group through m_buf and the m_full barriers; each group keeps its own
+    // row sum.
     const int grp = warp >> 2;
     const int wq = warp & 3;                   // TMEM lane quarter
     const int row = wq * 32 + lane;            // query row == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t pair_barrier = 1 + wq;      // the two warps (one per group) of these lanes
+    const uint32_t pair_barrier = 1 + wq;      // the warps (one per group) of these lanes
     const bool warp_active = (BK == 128) || (wq < 2);
     const int64_t token = static_cast<int64_t>(qb) * BK + row;
     const bool row_valid = warp_active && row < BK && token < a.tokens;
@@ -304,18 +331,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float l = 0.f;                      // this group's row sum, relative to m_mine
     bool ok = true;
     int kb_next = (warp_active && grp < n) ? block_id(grp) : 0;
-    for (int j = grp; ok && j < n; j += 2) {
+    for (int j = grp; ok && j < n; j += kGroups) {
       const int sb = j % kSBuffers;
       ok = mbar_wait(&bar->s_full[sb], (j / kSBuffers) & 1, abort_flag, a.err_word);
       if (!ok) break;
       tc_fence_after();
       const uint32_t sbuf = tmem + lane_addr + sb * 128;
       const int kb = kb_next;
-      if (warp_active && j + 2 < n) kb_next = block_id(j + 2);  // hide the next id's latency
+      if (warp_active && j + kGroups < n) kb_next = block_id(j + kGroups);  // hide its latency
       const int64_t valid = a.tokens - static_cast<int64_t>(kb) * BK;
       const bool partial = valid < BK;
-      uint32_t keep[kKeptChunks<BK>][32];
-      const float mrow = warp_active ? row_max<BK>(sbuf, partial, valid, keep) * c : -INFINITY;
+      uint32_t keep[kKeep<BK>][32];
+      const float mrow =
+          warp_active ? row_max<BK, kKeep<BK>, kRegSplit>(sbuf, partial, valid, keep) * c
+                      : -INFINITY;
       // The previous block's stabiliser (decided by the other group).
       float m_prev = -INFINITY;
       if (j > 0) {
@@ -332,8 +361,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_mine = m_used;
         const float2 neg_m = make_float2(-m_used, -m_used);
         // Partial blocks (masked columns) take every exponential on MUFU.
-        const float2 rs = partial ? row_exp<BK, 0>(sbuf, true, valid, c2, neg_m, keep)
-                                  : row_exp<BK, kEmulatedPairsPer8>(sbuf, false, valid, c2, neg_m, keep);
+        const float2 rs =
+            partial ? row_exp<BK, 0, kKeep<BK>>(sbuf, true, valid, c2, neg_m, keep)
+                    : row_exp<BK, kEmulatedPairsPer8, kKeep<BK>>(sbuf, false, valid, c2, neg_m, keep);
         l += rs.x + rs.y;
         if constexpr (kDenseMass) {
           if (row_valid) {
@@ -370,19 +400,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_arrive(&bar->p_full[sb]);
     }
     // ---------------------------------------------------------- epilogue
-    // Both groups' (stabiliser, sum) meet through shared memory; the final
-    // stabiliser is the larger one (it never decreases along the blocks).
-    // Group g then writes output features [64 g, 64 g + 64).
+    // All groups' (stabiliser, sum) meet through shared memory; the final
+    // stabiliser is the largest (it never decreases along the blocks).
+    // Groups 0 and 1 then write output features [64 g, 64 g + 64).
     float* xs = sX;  // [group][row] stabilisers, then [group][row] sums
-    named_bar_sync(pair_barrier, 64);    // both groups are past their last m_buf read
+    named_bar_sync(pair_barrier, 32 * kGroups);    // every group is past its last m_buf read
     xs[grp * 128 + row] = m_mine;
-    xs[256 + grp * 128 + row] = l;
-    named_bar_sync(pair_barrier, 64);
-    const float m_o = xs[(grp ^ 1) * 128 + row];
-    const float l_o = xs[256 + (grp ^ 1) * 128 + row];
-    const float m_fin = fmaxf(m_mine, m_o);
-    const float l_row = (m_mine == -INFINITY ? 0.f : l * ex2_approx(m_mine - m_fin)) +
-                        (m_o == -INFINITY ? 0.f : l_o * ex2_approx(m_o - m_fin));
+    xs[kGroups * 128 + grp * 128 + row] = l;
+    named_bar_sync(pair_barrier, 32 * kGroups);
+    float m_fin = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) m_fin = fmaxf(m_fin, xs[g * 128 + row]);
+    float l_row = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {
+      const float m_g = xs[g * 128 + row];
+      if (m_g != -INFINITY) l_row += xs[kGroups * 128 + g * 128 + row] * ex2_approx(m_g - m_fin);
+    }
     if (ok && n > 0) {
       ok = mbar_wait(&bar->o_done[(n - 1) % kSBuffers], ((n - 1) / kSBuffers) & 1, abort_flag,
                      a.err_word);
@@ -398,7 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         row_store = false;
       }
     }
-    if (warp_active) {
+    if (warp_active && grp < 2) {
       __nv_bfloat16* out = a.out + b * a.out_stride_b + out_token * a.out_stride_t +
                            h * a.out_stride_h + grp * 64;
       const float inv_l = (n > 0 && l_row > 0.f) ? 1.f / l_row : 0.f;
@@ -460,6 +494,13 @@ cudaError_t launch_bk(const CUtensorMap& tq, const CUtensorMap& tk, const CUtens
     if (e != cudaSuccess) return e;
     bytes = optin < L::kUsed + 1024 ? optin : L::kUsed + 1024;
     if (bytes < L::kUsed) return cudaErrorInvalidConfiguration;
+    if constexpr (kRegSplit) {
+      // The register split assumes exactly kLaunchRegs per thread at launch.
+      cudaFuncAttributes attr{};
+      e = cudaFuncGetAttributes(&attr, bsa_attention_kernel<BK, kDenseMass>);
+      if (e != cudaSuccess) return e;
+      if (attr.numRegs != static_cast<int>(kLaunchRegs)) return cudaErrorInvalidConfiguration;
+    }
     e = cudaFuncSetAttribute(bsa_attention_kernel<BK, kDenseMass>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;

@@ -72,7 +72,10 @@ constexpr int kKeptChunks = BK == 128 ? 2 : 1;
 // First pass: the row max (raw scores) of the BK-column S row at sbuf, all
 // chunks loaded at once; the last kKeptChunks chunks stay in `keep` (masked)
 // for the second pass.
-template <int BK, int kKeep = kKeptChunks<BK>>
+// kBatched: the chunks re-read later are loaded and reduced first (one TMEM
+// wait), then the kept ones (a second wait), so at most half a row is live at
+// once (for register budgets below a full row plus working set).
+template <int BK, int kKeep = kKeptChunks<BK>, bool kBatched = false>
 __device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t valid,
                                          uint32_t (&keep)[kKeep][32]) {
   constexpr int kChunks = BK / 32;
@@ -83,11 +86,20 @@ __device__ __forceinline__ float row_max(uint32_t sbuf, bool partial, int64_t va
   for (int q = 0; q < 8; ++q) m8[q] = -INFINITY;
 #pragma unroll
   for (int k = 0; k < kFirst; ++k) tmem_ld_32x32b_x32(sbuf + k * 32, r[k]);
+  if constexpr (kBatched) {
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < kFirst; ++k) {
+      reg_fence<32>(r[k]);
+      if (partial) mask_chunk(r[k], k * 32, valid);
+      max_chunk(m8, r[k]);
+    }
+  }
 #pragma unroll
   for (int k = 0; k < kKeep; ++k) tmem_ld_32x32b_x32(sbuf + (kFirst + k) * 32, keep[k]);
   tmem_wait_ld();
 #pragma unroll
-  for (int k = 0; k < kFirst; ++k) {
+  for (int k = 0; k < (kBatched ? 0 : kFirst); ++k) {
     reg_fence<32>(r[k]);
     if (partial) mask_chunk(r[k], k * 32, valid);
     max_chunk(m8, r[k]);

@@ -167,7 +167,7 @@ def test_pipelined_exchange_equals_full_attention():
 
 
 def test_pipeline_chunk_rule():
-    assert [parallel.pipeline_chunks(h) for h in (40, 20, 10, 5, 8, 12, 3)] == [5, 5, 5, 1, 4, 4, 1]
+    assert [parallel.pipeline_chunks(h) for h in (40, 20, 10, 5, 8, 12, 3)] == [4, 4, 2, 1, 2, 2, 1]
     with pytest.raises(ValueError):
         parallel.PipelinedHeadParallel(None, 2, 40, 16, chunks=3)
     with pytest.raises(ValueError):
