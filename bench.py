@@ -679,8 +679,9 @@ def run_forward5(args):
     (``README.md:46-54``: sampled bootstrap, sampled update every 2 steps,
     dense dispatch at keep >= 0.58); and the same backend with the dense
     threshold off, so every route after layer 0 / step 0 runs sparse.  Each is
-    warmed up with one step, then timed from the first transformer call to the
-    last scheduler update with CUDA events (max over ranks)."""
+    warmed up with three steps (first use of every collective included), then
+    timed from the first transformer call to the last scheduler update with
+    CUDA events (max over ranks)."""
     import torch.distributed as dist
 
     from dit_sparse_atten_b200 import _native, parallel, wan_model
@@ -753,7 +754,9 @@ def run_forward5(args):
     results = {}
     with ClockSampler(local) as clocks:
         for name, make in variants.items():
-            timed(make, 1)                     # warm-up: one step, fresh state
+            # warm-up: three steps with a fresh state, so the route bootstrap,
+            # its adoption (the keep all-reduce) and an update have all run once
+            timed(make, 3)
             seconds, step_ms, summary, finite = timed(make, 5)
             results[name] = {"forward_5step_s": seconds,
                              "step_ms_rank0": [round(x, 1) for x in step_ms],
@@ -764,7 +767,7 @@ def run_forward5(args):
                                             "dense_dispatched_routes", "released_routes")}
     line = {
         "metric": METRIC, "value": results["flex_reuse"]["forward_5step_s"], "unit": "s",
-        "n_gpus": world, "steps": 5, "warmup": 1, "higher_is_better": False,
+        "n_gpus": world, "steps": 5, "warmup": 3, "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init Wan2.1-14B weights, seeded latent and text)",
         "config": {"workload": "config5_wan14b_5step_forward: 57,600 tokens, CFG on, "
