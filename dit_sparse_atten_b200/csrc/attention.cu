@@ -417,9 +417,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float m_g = xs[g * 128 + row];
       if (m_g != -INFINITY) l_row += xs[kGroups * 128 + g * 128 + row] * ex2_approx(m_g - m_fin);
     }
+    // O is final once every PV has completed: drain[1] (one phase) is the PV
+    // issuer's commit after its last MMA.  (A wait on o_done of the last
+    // block could return early for a group that last saw that barrier two
+    // phases back.)
     if (ok && n > 0) {
-      ok = mbar_wait(&bar->o_done[(n - 1) % kSBuffers], ((n - 1) / kSBuffers) & 1, abort_flag,
-                     a.err_word);
+      ok = mbar_wait(&bar->drain[1], 0, abort_flag, a.err_word);
       tc_fence_after();
     }
     // Destination token of this row (the unpack folded into the store).
