@@ -724,6 +724,8 @@ def run_forward5(args):
         reset_runtime_state()
 
         def attention(q, k, v):
+            if isinstance(backend, FlexReuseBackend):
+                return backend.head_parallel(q, k, v, shard.group, P)
             return parallel.head_parallel_attention(q, k, v, lambda a, b, c: backend(a, b, c),
                                                     shard.group, P)
         step_ms = []
@@ -1053,11 +1055,7 @@ def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total
             stream.wait_event(ready)
             set_routing_context(attention_id=1, step=1, branch=b, grid=cfg.grid)
             qi, ki, vi = (x.unsqueeze(0) for x in bufs)
-            if P > 1:
-                out = parallel.head_parallel_attention(qi, ki, vi, lambda a, b_, c: backend(a, b_, c),
-                                                       group, P)
-            else:
-                out = backend(qi, ki, vi)
+            out = backend.head_parallel(qi, ki, vi, group, P)
             done = torch.cuda.Event()
             done.record(stream)
             slot_free[slot][bi] = done
@@ -1090,7 +1088,8 @@ def run_e2e(args, cfg, plan, group, branches, local_route, layout, device, total
     return {"value": total_flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": per_rank_in * world,
             "d2h_bytes_per_step": out_host.numel() * out_host.element_size() * world,
-            "api": "FlexReuseBackend.__call__ (reuse phase, spatial reorder) per CFG branch; "
+            "api": "FlexReuseBackend.head_parallel (reuse phase, spatial reorder; head chunks "
+                   "overlapped with the exchange for P > 1) per CFG branch; "
                    "H2D/D2H on side streams overlapping compute (every step copies its own "
                    "inputs in and its output out)"}
 

@@ -364,6 +364,7 @@ class FlexReuseBackend:
         self.state = _StateTable()
         self.route_streams = {}
         self.spatial_layouts = {}
+        self.pipelines = {}
         self.log = PhaseLog()
 
     @property
@@ -704,6 +705,85 @@ class FlexReuseBackend:
         if self._final_step(step):
             self._release(key)
         return unpacked(output)
+
+    # ------------------------------------------------------------ multi-GPU
+    def head_parallel(self, q, k, v, group, group_size, rows=None, chunks=None, **call_kw):
+        """This backend over the head shards of sequence-sharded inputs.
+
+        ``q, k, v``: ``[1, T/P, H, D]`` (one CFG branch of a sequence-parallel
+        caller, ``P = group_size`` ranks in ``group``); returns the output
+        shard ``[1, T/P, H, D]``.  A sparse-reuse call -- the common one --
+        exchanges the heads in chunks overlapped with the attention
+        (``parallel.PipelinedHeadParallel``): chunk c's heads attend over
+        their slice of the layer's CSR route, packed by the exchange's row
+        gather and stored back to token order into the output exchange's send
+        buffer.  Every other call (bootstrap, refreshes, updates, dense
+        dispatch, non-default arguments) exchanges all heads at once
+        (``parallel.head_parallel_attention``) and runs ``__call__``.
+        ``call_kw`` are ``__call__``'s keyword arguments.
+        """
+        from . import parallel
+
+        if group_size == 1:
+            return self(q, k, v, **call_kw)
+        plan = self._reuse_plan(q, k, v, group_size, call_kw)
+        if plan is None:
+            return parallel.head_parallel_attention(
+                q, k, v, lambda a, b, c: self(a, b, c, **call_kw), group, group_size, rows=rows)
+        key, step, layout, state = plan
+        heads = q.shape[2]
+        pkey = (id(group), group_size, heads, q.shape[1], q.device,
+                layout.signature if layout is not None else None, chunks)
+        pipe = self.pipelines.get(pkey)
+        if pipe is None:
+            perm = layout.permutation_cpu if layout is not None else None
+            inverse = layout.inverse_cpu if layout is not None else None
+            pipe = parallel.PipelinedHeadParallel(group, group_size, heads, q.shape[1], perm,
+                                                  inverse, chunks=chunks, rows=rows)
+            self.pipelines[pkey] = pipe
+        counts, indices = state.block_mask.counts[0], state.block_mask.indices[0]
+        hc = pipe.hc
+        scale = call_kw.get("softmax_scale")
+
+        def attend(qp, kp, vp, chunk, out, out_rows):
+            hs = slice(chunk * hc, (chunk + 1) * hc)
+            kernels.block_sparse_attention(qp, kp, vp, counts[hs], indices[hs],
+                                           block=self.config.block_size, scale=scale, out=out,
+                                           out_rows=out_rows)
+
+        out = pipe(q, k, v, attend)
+        self.log.hit("sparse_reuse")
+        if self._final_step(step):
+            self._release(key)
+        return out
+
+    def _reuse_plan(self, q, k, v, group_size, call_kw):
+        """(key, step, layout, state) when the head-sharded call of these
+        sequence shards is a plain sparse reuse, else None."""
+        if set(call_kw) - {"softmax_scale", "dtype"}:
+            return None
+        if call_kw.get("dtype", torch.bfloat16) != q.dtype or q.dtype != torch.bfloat16:
+            return None
+        if not (q.shape == k.shape == v.shape and q.shape[0] == 1):
+            return None
+        b, t_local, h, d = q.shape
+        if h % group_size:
+            return None
+        attention_id, step, branch, grid = self._context()
+        if self.config.first_layer_dense and attention_id == 0:
+            return None
+        tokens = t_local * group_size
+        layout = self._spatial_layout(grid, tokens)
+        if self.config.spatial_reorder and layout is None:
+            return None
+        key = (attention_id, branch, tokens, h // group_size, d, q.device,
+               layout.signature if layout is not None else None)
+        if self._plan(key, step) != "reuse":
+            return None
+        state = self.state[key]
+        if not isinstance(state.block_mask, BlockRoute):
+            return None
+        return key, step, layout, state
 
     def _bootstrap(self, key, step, layout, grid, q, k, v, softmax_scale, dense_kw):
         """Step 0 (or a new key): dense output plus the first route, exact

@@ -1,10 +1,10 @@
 """Head-parallel exchange on real GPUs (NCCL), when the box has two or more.
 
-Two ranks hold sequence shards of one branch; both exchange paths - the
-unchunked ``head_parallel_attention`` (the backend API's path) and the
-chunked ``PipelinedHeadParallel`` with the routed kernel storing into the
-output all-to-all's send buffer - must give the single-GPU result on every
-row of the rank's shard.  Skipped with fewer than two GPUs; the host-side
+Two ranks hold sequence shards of one branch; every exchange path - the
+unchunked ``head_parallel_attention``, the chunked ``PipelinedHeadParallel``
+with the routed kernel storing into the output all-to-all's send buffer, and
+the public ``FlexReuseBackend.head_parallel`` on a reuse call - must give the
+single-GPU result on every row of the rank's shard.  Skipped with fewer than two GPUs; the host-side
 layout logic is covered on CPU by tests/test_parallel_gloo.py.
 """
 
@@ -29,6 +29,8 @@ def _worker(rank, world, port, queue):
     from datetime import timedelta
 
     from dit_sparse_atten_b200 import _native, kernels, parallel
+    from dit_sparse_atten_b200.context import set_routing_context
+    from dit_sparse_atten_b200.flex import FlexReuseBackend, FlexReuseConfig
     from dit_sparse_atten_b200.spatial import build_spatial_layout
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -76,9 +78,18 @@ def _worker(rank, world, port, queue):
 
         out2 = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
                     attend_chunk)
+        # the public API: FlexReuseBackend.head_parallel on a reuse call
+        backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True))
+        backend.install_route(route[hs].to(dev), attention_id=1, branch=0, tokens=T, heads=hp,
+                              head_dim=128, device=dev, grid=grid)
+        set_routing_context(attention_id=1, step=1, branch=0, grid=grid)
+        out3 = backend.head_parallel(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                     v[:, sl].contiguous(), dist.group.WORLD, world, chunks=2)
         torch.cuda.synchronize()
         _native.check_device_errors()
+        assert backend.pipelines and backend.phase_counts["sparse_reuse"] == 1
         errs.append(float((out2.float() - ref[:, sl].float()).abs().max()))
+        errs.append(float((out3.float() - ref[:, sl].float()).abs().max()))
         queue.put((rank, errs))
     except Exception as exc:
         queue.put((rank, repr(exc)))
@@ -101,4 +112,4 @@ def test_exchange_paths_match_single_gpu():
     for rank, errs in results.items():
         assert not isinstance(errs, str), errs
         # the same kernels on the same rows: the exchange must not change a bit
-        assert errs == [0.0, 0.0], (rank, errs)
+        assert errs == [0.0, 0.0, 0.0], (rank, errs)

@@ -147,6 +147,81 @@ def _pipelined(rank, world):
     return True
 
 
+def cpu_block_sparse_attention(q, k, v, counts, indices, block=128, scale=None, out=None,
+                               return_lse=False, out_rows=None):
+    """fp32 CPU stand-in for ``kernels.block_sparse_attention`` (same
+    arguments and output placement) for the host-side tests."""
+    B, T, H, D = q.shape
+    scale = scale or D ** -0.5
+    res = torch.empty_like(q)
+    for h in range(H):
+        for qb in range(counts.shape[-1]):
+            n = int(counts[h, qb])
+            keys = torch.cat([torch.arange(kb * block, min((kb + 1) * block, T))
+                              for kb in indices[h, qb, :n].tolist()])
+            rows = torch.arange(qb * block, min((qb + 1) * block, T))
+            s = q[0, rows, h].float() @ k[0, keys, h].float().T * scale
+            res[0, rows, h] = (torch.softmax(s, -1) @ v[0, keys, h].float()).to(q.dtype)
+    dst = out if out is not None else torch.empty_like(q)
+    if out_rows is not None:
+        dst[:, out_rows.long()] = res
+    else:
+        dst.copy_(res)
+    return dst
+
+
+def cpu_pack_boolean_rows(route):
+    counts = route.sum(-1).to(torch.int32)
+    order = torch.argsort((~route).to(torch.int8), dim=-1, stable=True)
+    return counts, order.to(torch.int32)
+
+
+def _backend_head_parallel(rank, world):
+    """FlexReuseBackend.head_parallel on a reuse call: the chunked, overlapped
+    exchange gives the same output as all heads through __call__ and as the
+    unsharded routed attention; other calls take the unchunked exchange."""
+    from dit_sparse_atten_b200 import flex, kernels
+    from dit_sparse_atten_b200.context import set_routing_context
+    from dit_sparse_atten_b200.flex import FlexReuseBackend, FlexReuseConfig
+
+    kernels.block_sparse_attention = cpu_block_sparse_attention
+    kernels.pack_boolean_rows = cpu_pack_boolean_rows
+    kernels.reorder_rows = lambda tensors, perm: tuple(x.index_select(1, perm.long())
+                                                       for x in tensors)
+    flex.frontier_mask = lambda route, neighbors: None
+    grid, heads, d = (2, 16, 16), 4, 16
+    tokens = 512
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn((1, tokens, heads, d), generator=g).to(torch.bfloat16)
+               for _ in range(3))
+    route = torch.rand((heads, 4, 4), generator=g) < 0.6
+    route[:, torch.arange(4), torch.arange(4)] = True
+    t = tokens // world
+    sl = slice(rank * t, (rank + 1) * t)
+    hp = heads // world
+    backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True))
+    backend.install_route(route[rank * hp:(rank + 1) * hp], attention_id=1, branch=0,
+                          tokens=tokens, heads=hp, head_dim=d, device=torch.device("cpu"),
+                          grid=grid)
+    set_routing_context(attention_id=1, step=1, branch=0, grid=grid)
+    shard = [x[:, sl].contiguous() for x in (q, k, v)]
+    piped = backend.head_parallel(*shard, dist.group.WORLD, world, rows=CpuRows, chunks=2)
+    assert backend.pipelines, "reuse call must take the chunked exchange"
+    assert backend.phase_counts["sparse_reuse"] == 1
+    plain = backend.head_parallel(*shard, dist.group.WORLD, world, rows=CpuRows,
+                                  deterministic=True)    # not the pipelined form
+    assert backend.phase_counts["sparse_reuse"] == 2 and len(backend.pipelines) == 1
+    # unsharded: pack, routed attention over all heads, unpack
+    layout = backend._spatial_layout(grid, tokens)
+    perm = layout.permutation_cpu.long()
+    counts, indices = cpu_pack_boolean_rows(route)
+    ref = cpu_block_sparse_attention(q[:, perm], k[:, perm], v[:, perm], counts, indices,
+                                     out_rows=perm)
+    torch.testing.assert_close(piped, ref[:, sl], atol=2e-2, rtol=0)
+    torch.testing.assert_close(plain, piped, atol=2e-2, rtol=0)
+    return True
+
+
 def _keep(rank, world):
     from dit_sparse_atten_b200.flex import FlexReuseBackend
     backend = FlexReuseBackend(process_group=dist.group.WORLD)
@@ -164,6 +239,10 @@ def test_head_parallel_attention_equals_full():
 
 def test_pipelined_exchange_equals_full_attention():
     assert all(run_ranks(_pipelined).values())
+
+
+def test_backend_head_parallel_pipelines_reuse_calls():
+    assert all(run_ranks(_backend_head_parallel).values())
 
 
 def test_pipeline_chunk_rule():
