@@ -398,6 +398,7 @@ int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64_t batch
 int64_t bsa_sampled_mass_workspace_bytes(int64_t batch, int64_t heads, int32_t q_blocks,
                                          int32_t samples) {
   if (batch <= 0 || heads <= 0 || q_blocks <= 0 || samples <= 0) return 0;
+  if (bsa::sampled_mass_on_chip(q_blocks, samples)) return 0;   // kept on chip
   const int64_t n_rows = static_cast<int64_t>(q_blocks) * samples;
   return batch * heads * n_rows * (static_cast<int64_t>(q_blocks) + 1) * 4;
 }
@@ -408,10 +409,10 @@ int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_k, int64
                              float* workspace, int64_t workspace_bytes, float* mass,
                              int32_t* err_word, void* stream) {
   const int64_t need = bsa_sampled_mass_workspace_bytes(batch, heads, q_blocks, samples);
-  if (workspace == nullptr || workspace_bytes < need)
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(BSA_ERR_INVALID_ARGUMENT, "workspace of %lld bytes needed (got %lld)",
                 static_cast<long long>(need), static_cast<long long>(workspace_bytes));
-  if (reinterpret_cast<uintptr_t>(workspace) & 15)
+  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 15))
     return fail(BSA_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
   if (batch * heads > 65535) return fail(BSA_ERR_UNSUPPORTED, "batch * heads must be <= 65535");
   CUtensorMap tq, tk;
@@ -421,6 +422,11 @@ int bsa_sampled_mass_onepass(const void* sampled_q, const void* sampled_k, int64
                                     &tk, &a);
   if (rc != BSA_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bsa::sampled_mass_on_chip(q_blocks, samples)) {
+    cudaError_t e = bsa::launch_sampled_mass_on_chip(tq, tk, a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bsa_sampled_mass_onepass launch");
+    return ok();
+  }
   if (samples <= 2) {
     // One or two keys per block: the two-pass kernel (the workspace is unused).
     cudaError_t e = bsa::launch_sampled_mass(tq, tk, a, s);

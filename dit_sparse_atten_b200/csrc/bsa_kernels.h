@@ -115,6 +115,12 @@ cudaError_t launch_sampled_mass(const CUtensorMap& tm_q, const CUtensorMap& tm_k
 // mass[b, h, qb, kb] = mass_scale * sum_{s < S} 2^(block_lse[b, h, kb, qb S + s]
 //                                                 - row_lse[b, h, qb S + s])
 cudaError_t launch_sampled_mass_reduce(const MassArgs& args, cudaStream_t stream);
+// One pass with the per-block sums kept in TMEM and shared memory (no
+// workspace, no reduction launch): 16 or 32 samples and up to 473 blocks
+// (sampled_mass_on_chip); block_lse and lse must be null.
+bool sampled_mass_on_chip(int32_t q_blocks, int32_t samples);
+cudaError_t launch_sampled_mass_on_chip(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                        const MassArgs& args, cudaStream_t stream);
 
 // ---- (b) sampled block mass without a caller workspace ---------------------
 // Size of the module-level scratch (a static __device__ array) that

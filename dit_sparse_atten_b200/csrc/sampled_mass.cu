@@ -31,8 +31,6 @@ constexpr float kLog2eM = 1.4426950408889634f;
 constexpr int kQBytes = kTile * 256;
 constexpr int kSlotBytes = kTile * 256;
 constexpr int kPanel = kTile * 128;
-constexpr int kRingOff = kQBytes;
-constexpr int kBiasOff = kRingOff + kSlots * kSlotBytes;
 constexpr int kMaxBlocks = 4096;
 
 struct MassBarriers {
@@ -67,10 +65,28 @@ struct MassBarriers {
 // (red_full / red_free, double-buffered).  After the softmax warps: the TMA
 // producer warp, then the TMEM allocator + tcgen05.mma issuer warp.
 constexpr int kRedTiles = 16;
-constexpr int kXchgOff = kBiasOff + kMaxBlocks * 4;
-constexpr int kRedOff = kXchgOff + 4 * 128 * 2 * 4;           // [2][kRedTiles][8] floats
-constexpr int kBar2Off = kRedOff + 2 * kRedTiles * 8 * 4;
-constexpr int kMass2Smem = kBar2Off + 256 + 1024;
+
+// Shared-memory layout.  kOnChip (one pass, the per-block log sums kept on
+// chip instead of a workspace): a two-slot K ring, and after the barriers a
+// [block - kTmemVals][row] float area for the blocks past the first
+// kTmemVals, whose values live in TMEM columns 256 + block.
+template <bool kOnChip>
+struct MassLayout {
+  static constexpr int kRingSlots = kOnChip ? 2 : kSlots;
+  static constexpr int kRing = kQBytes;
+  static constexpr int kBias = kRing + kRingSlots * kSlotBytes;
+  static constexpr int kXchg = kBias + kMaxBlocks * 4;
+  static constexpr int kRed = kXchg + 4 * 128 * 2 * 4;          // [2][kRedTiles][8] floats
+  static constexpr int kBar = kRed + 2 * kRedTiles * 8 * 4;
+  static constexpr int kVals = kBar + 256;
+  static constexpr int kBytes = kVals + 1024;                   // + base alignment slack
+};
+constexpr int kTmemVals = 256;     // on-chip mode: block log sums in TMEM columns [256, 512)
+constexpr int kMaxDynSmem = 232448;
+// Blocks the on-chip mode holds: TMEM, then shared memory (473 at 227 KB).
+constexpr int kOnChipMaxBlocks =
+    kTmemVals + (kMaxDynSmem - MassLayout<true>::kBytes) / (128 * 4);
+constexpr int kMass2Smem = MassLayout<false>::kBytes;
 constexpr int kMassEmulated = 2;  // of every 8 column pairs, exponentials on the FMA pipe
 
 // Warp layout.  S = 16, 32: sixteen softmax warps, four per SM sub-partition,
@@ -173,7 +189,64 @@ __device__ __forceinline__ void mass_scores_scaled(const uint32_t* r, float2* v,
 // error on the fewest terms.
 constexpr int kOnePassEmulated = 1;
 
-template <int LOG2S, bool kRound>
+// The sum of S values over S consecutive lanes, for S values at once:
+// afterwards x[0] of lane l is the sum over its S-lane group of value
+// (l mod S) (a butterfly that halves the values kept at each step).
+template <int S>
+__device__ __forceinline__ void lane_group_sums(float (&x)[S]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int half = S / 2; half >= 1; half >>= 1) {
+    const bool up = (lane & half) != 0;
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float send = up ? x[j] : x[j + half];
+      const float keep = up ? x[j + half] : x[j];
+      x[j] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+    }
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&x)[N]) {
+  uint32_t r[32];
+  if constexpr (N == 32) {
+    tmem_ld_32x32b_x32(taddr, r);
+  } else if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+  } else {
+    static_assert(N == 4, "4, 8, 16 or 32 columns");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+  }
+  tmem_wait_ld();
+  reg_fence<N>(r);
+#pragma unroll
+  for (int j = 0; j < N; ++j) x[j] = __uint_as_float(r[j]);
+}
+
+// kOnChip: one pass with no workspace.  Each sampled row keeps the log2 of
+// its exponential sum over every key block (running stabiliser folded in) in
+// TMEM columns 256 + block (the first kTmemVals blocks) and in shared memory
+// (the rest); once the row's log-sum-exp is known the CTA forms the mass of
+// its S-row query blocks itself: 2^(block value - row), summed over the S
+// rows (lanes) of each query block, times 1/S.
+template <int LOG2S, bool kRound, bool kOnChip = false>
 __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
     sampled_mass_kernel2(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k, const MassArgs a) {
@@ -188,12 +261,15 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  using L = MassLayout<kOnChip>;
+  constexpr int kRing = L::kRingSlots;
   uint8_t* sQ = smem;
-  uint8_t* sRing = smem + kRingOff;
-  float* sBiasL = reinterpret_cast<float*>(smem + kBiasOff);
-  float2* sX = reinterpret_cast<float2*>(smem + kXchgOff);  // [part][row] (max, sum)
-  float* sRed = reinterpret_cast<float*>(smem + kRedOff);    // [buf][tile][warp] (S > 32)
-  MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + kBar2Off);
+  uint8_t* sRing = smem + L::kRing;
+  float* sBiasL = reinterpret_cast<float*>(smem + L::kBias);
+  float2* sX = reinterpret_cast<float2*>(smem + L::kXchg);  // [part][row] (max, sum)
+  float* sRed = reinterpret_cast<float*>(smem + L::kRed);    // [buf][tile][warp] (S > 32)
+  MassBarriers* bar = reinterpret_cast<MassBarriers*>(smem + L::kBar);
+  float* sVals = reinterpret_cast<float*>(smem + L::kVals);  // kOnChip: [block - 256][row]
   volatile int* abort_flag = &bar->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -207,9 +283,11 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
   // (S <= 2 has one or two keys per block: the per-block state of one-pass
   // mode would not fit the registers, so those take two passes.)
   constexpr bool kOnePass = !kWide && LOG2S >= 2;
+  static_assert(!kOnChip || kOnePass, "on-chip mode is one-pass");
   const bool emit = kOnePass && a.block_lse != nullptr;
+  const bool one = emit || kOnChip;           // a single pass over the keys
   const int pass1 = a.lse != nullptr ? 0 : n_tiles;
-  const int steps = emit ? n_tiles : pass1 + n_tiles;
+  const int steps = one ? n_tiles : pass1 + n_tiles;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
@@ -220,7 +298,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
       mbar_init(&bar->red_free[i], 1);
     }
     mbar_init(&bar->drain, 1);
-    for (int s = 0; s < kSlots; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&bar->slot_full[s], 1);
       mbar_init(&bar->slot_empty[s], 1);
     }
@@ -231,7 +309,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
   if (bar->abort) return;  // uniform: set before the barrier, read after it
   for (int i = threadIdx.x; i < a.q_blocks; i += Shape::kThreads)
     sBiasL[i] = a.block_bias != nullptr ? a.block_bias[i] * kLog2eM : 0.f;
-  if (warp == Shape::kMmaWarp) tmem_alloc(&bar->tmem_base, 256);
+  if (warp == Shape::kMmaWarp) tmem_alloc(&bar->tmem_base, kOnChip ? 512 : 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -246,8 +324,8 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
       tma_load_4d(sQ + kPanel, &tm_q, &bar->q_full, 64, h, qt * kTile, b);
       uint32_t armed = 0, armed_phase = 0;
       for (int i = 0; i < steps; ++i) {
-        const int s = i % kSlots;
-        const uint32_t ph = (i / kSlots) & 1;
+        const int s = i % kRing;
+        const uint32_t ph = (i / kRing) & 1;
         if (!mbar_wait(&bar->slot_empty[s], ph ^ 1, abort_flag, a.err_word)) break;
         const int kt = i % n_tiles;
         uint8_t* dst = sRing + s * kSlotBytes;
@@ -260,7 +338,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
       int never = 0;
       mbar_wait(&bar->q_full, 0, &never, a.err_word);
 #pragma unroll
-      for (int s = 0; s < kSlots; ++s)
+      for (int s = 0; s < kRing; ++s)
         if (armed & (1u << s)) mbar_wait(&bar->slot_full[s], (armed_phase >> s) & 1u, &never, a.err_word);
     }
   } else if (warp == Shape::kMmaWarp) {
@@ -270,8 +348,8 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
       const uint64_t kdesc0 = sdesc_sw128(smem_u32(sRing), 16, 1024);
       bool ok = mbar_wait(&bar->q_full, 0, abort_flag, a.err_word);
       for (int i = 0; ok && i < steps; ++i) {
-        const int s = i % kSlots;
-        ok = mbar_wait(&bar->slot_full[s], (i / kSlots) & 1, abort_flag, a.err_word);
+        const int s = i % kRing;
+        ok = mbar_wait(&bar->slot_full[s], (i / kRing) & 1, abort_flag, a.err_word);
         if (ok && i >= 2) ok = mbar_wait(&bar->s_free[i & 1], ((i >> 1) - 1) & 1, abort_flag, a.err_word);
         if (!ok) break;
         tc_fence_after();
@@ -315,7 +393,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar->s_free[i & 1]);
       const int64_t key0 = static_cast<int64_t>(i % n_tiles) * kTile + part * kCols;
-      if (kOnePass && emit) {
+      if (kOnePass && one) {
         // One pass.  Stabiliser: the running max of (score * log2 e + the
         // largest block bias of this part), an upper bound of every argument,
         // so each exponential's argument is a single FMA with a per-block
@@ -344,7 +422,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
         const float m_new = fmaxf(m2, m_tile);
         if (m_new != -INFINITY) {
           const float2 l2e = make_float2(kLog2eM, kLog2eM);
-          float* dst = a.block_lse + (out_rows + kb0) * a.n_rows + qrow;
+          float* dst = kOnChip ? nullptr : a.block_lse + (out_rows + kb0) * a.n_rows + qrow;
           const bool write = qrow < a.n_rows;
           float tot = 0.f;
           constexpr int kBlockPairs = S / 2;
@@ -362,7 +440,16 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
             }
             const float g = acc.x + acc.y;
             tot += g;
-            if (write && kb0 + gi < a.q_blocks) dst[gi * a.n_rows] = m_new + __log2f(g);
+            const float val = m_new + __log2f(g);
+            if constexpr (kOnChip) {
+              const int kb = static_cast<int>(kb0) + gi;     // the same for the whole warp
+              if (kb < kTmemVals)
+                tmem_st_32x32b_x1(tmem + lane_addr + kTmemVals + kb, __float_as_uint(val));
+              else if (kb < a.q_blocks)
+                sVals[(kb - kTmemVals) * 128 + row] = val;
+            } else if (write && kb0 + gi < a.q_blocks) {
+              dst[gi * a.n_rows] = val;
+            }
           }
           l = l * ex2_approx(m2 - m_new) + tot;
           m2 = m_new;
@@ -399,12 +486,17 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
           m2 = m_new;
         }
       }
-      if ((emit || i < pass1) && i == n_tiles - 1) {
+      if ((one || i < pass1) && i == n_tiles - 1) {
         {
           // End of the pass over the keys.  Combine the row's parts: the warps of these rows meet at named
           // barrier 1 + wq; every part adds the partial sums in part order.
           sX[part * 128 + row] = make_float2(m2, l);
+          if constexpr (kOnChip) {
+            tmem_wait_st();
+            tc_fence_before();
+          }
           asm volatile("bar.sync %0, %1;" ::"r"(1 + wq), "r"(32 * kParts) : "memory");
+          if constexpr (kOnChip) tc_fence_after();
           combined = true;
           float m_all, l_all;
           if constexpr (kParts == 2) {
@@ -426,6 +518,34 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
           m_fold = m_all + __log2f(l_all);
           if (emit && part == 0 && qrow < a.n_rows)
             a.row_lse[(static_cast<int64_t>(b) * a.heads + h) * a.n_rows + qrow] = m_fold;
+        }
+        if constexpr (kOnChip) {
+          // The mass of this CTA's query blocks: the warps of a lane quarter
+          // take groups of S key blocks in turn (group g by part g mod
+          // kParts), read the rows' block values, normalise them and sum
+          // each query block's S rows (lanes).
+          const bool vrow = qrow < a.n_rows;
+          const int64_t qblock = qrow >> LOG2S;
+          const int n_groups = (a.q_blocks + S - 1) / S;
+#pragma unroll 1
+          for (int g = part; g < n_groups; g += kParts) {
+            const int kbg = g * S;
+            float x[S];
+            if (kbg < kTmemVals) {
+              tmem_ld_cols<S>(tmem + lane_addr + kTmemVals + kbg, x);
+            } else {
+#pragma unroll
+              for (int j = 0; j < S; ++j)
+                x[j] = kbg + j < a.q_blocks ? sVals[(kbg + j - kTmemVals) * 128 + row] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < S; ++j)
+              x[j] = (vrow && kbg + j < a.q_blocks) ? ex2_approx(x[j] - m_fold) : 0.f;
+            lane_group_sums<S>(x);
+            const int kb = kbg + (lane & (S - 1));
+            if (kb < a.q_blocks && qblock < a.q_blocks)
+              a.mass[(out_rows + qblock) * a.q_blocks + kb] = x[0] * a.mass_scale;
+          }
         }
       }
       if (!emit && i >= pass1) {
@@ -528,7 +648,7 @@ __global__ void __launch_bounds__(MassShape<LOG2S>::kThreads, 1)
   __syncthreads();
   if (warp == Shape::kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, kOnChip ? 512 : 256);
   }
 }
 
@@ -587,33 +707,39 @@ __global__ void __launch_bounds__(256) sampled_mass_reduce_kernel(const MassArgs
   }
 }
 
-template <int LOG2S, bool kRound>
+template <int LOG2S, bool kRound, bool kOnChip>
 cudaError_t launch_log2s_v2(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                             cudaStream_t stream) {
   // Per-device flag; concurrent callers may both set the attribute, which is
-  // harmless, but the flag itself must not be a data race.
+  // harmless, but the flag itself must not be a data race.  The on-chip mode
+  // sets the largest size once; each launch asks for what its blocks need.
+  using L = MassLayout<kOnChip>;
   static std::atomic<bool> configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const int max_bytes = kOnChip ? kMaxDynSmem : L::kBytes;
   if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(sampled_mass_kernel2<LOG2S, kRound>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMass2Smem);
+    e = cudaFuncSetAttribute(sampled_mass_kernel2<LOG2S, kRound, kOnChip>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev].store(true, std::memory_order_release);
   }
+  int bytes = L::kBytes;
+  if (kOnChip && a.q_blocks > kTmemVals) bytes += (a.q_blocks - kTmemVals) * 128 * 4;
+  if (bytes > max_bytes) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>((a.n_rows + kTile - 1) / kTile),
                   static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  sampled_mass_kernel2<LOG2S, kRound>
-      <<<grid, MassShape<LOG2S>::kThreads, kMass2Smem, stream>>>(tq, tk, a);
+  sampled_mass_kernel2<LOG2S, kRound, kOnChip>
+      <<<grid, MassShape<LOG2S>::kThreads, bytes, stream>>>(tq, tk, a);
   return cudaGetLastError();
 }
 
-template <int LOG2S>
+template <int LOG2S, bool kOnChip = false>
 cudaError_t launch_s(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,
                            cudaStream_t stream) {
-  return a.round_bf16 ? launch_log2s_v2<LOG2S, true>(tq, tk, a, stream)
-                      : launch_log2s_v2<LOG2S, false>(tq, tk, a, stream);
+  return a.round_bf16 ? launch_log2s_v2<LOG2S, true, kOnChip>(tq, tk, a, stream)
+                      : launch_log2s_v2<LOG2S, false, kOnChip>(tq, tk, a, stream);
 }
 
 template <int LOG2S>
@@ -640,6 +766,22 @@ cudaError_t launch_sampled_mass_reduce(const MassArgs& a, cudaStream_t stream) {
     case 32: return launch_reduce_s<5>(a, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+bool sampled_mass_on_chip(int32_t q_blocks, int32_t samples) {
+  // S = 16, 32: four column parts of 32 keys; fewer samples per block keep
+  // more per-block state per thread than the on-chip pass has registers for.
+  return (samples == 16 || samples == 32) && q_blocks >= 1 && q_blocks <= kOnChipMaxBlocks;
+}
+
+cudaError_t launch_sampled_mass_on_chip(const CUtensorMap& tq, const CUtensorMap& tk,
+                                        const MassArgs& a, cudaStream_t stream) {
+  if (a.batch == 0 || a.heads == 0 || a.n_rows == 0) return cudaSuccess;
+  if (!sampled_mass_on_chip(a.q_blocks, a.samples) || a.lse != nullptr ||
+      a.block_lse != nullptr)
+    return cudaErrorInvalidValue;
+  return a.samples == 16 ? launch_s<4, true>(tq, tk, a, stream)
+                         : launch_s<5, true>(tq, tk, a, stream);
 }
 
 cudaError_t launch_sampled_mass(const CUtensorMap& tq, const CUtensorMap& tk, const MassArgs& a,

@@ -149,10 +149,12 @@ def sampled_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128, sampl
     """Sampled block mass ``[B, H, Qb, Qb]`` fp32 from bf16 ``q, k [B, T, H, D]``.
 
     Reference ``flex.py:205-251`` (per batch element).  ``one_pass`` streams
-    the sampled keys once (``bsa_sampled_mass_onepass``, with a workspace of
-    per-row block log-sums); otherwise every score is computed twice, once for
-    the row's log-sum-exp and once for the normalised block sums
-    (``bsa_sampled_mass``).
+    the sampled keys once (``bsa_sampled_mass_onepass``): with 16 or 32
+    samples and up to 473 blocks the per-row block log-sums stay on chip
+    (TMEM and shared memory) and the kernel writes the mass itself; other
+    shapes use a workspace and a reduction launch.  Otherwise every score is
+    computed twice, once for the row's log-sum-exp and once for the
+    normalised block sums (``bsa_sampled_mass``).
     """
     device = _require_cuda(q, k)
     if q.shape != k.shape or q.dim() != 4:
@@ -174,11 +176,12 @@ def sampled_block_mass(q: torch.Tensor, k: torch.Tensor, block: int = 128, sampl
     if one_pass and B * H <= 65535:
         lib = _native.load_library()
         nbytes = int(lib.bsa_sampled_mass_workspace_bytes(B, H, blocks, samples))
-        work = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        work = (torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=device)
+                if nbytes else None)
         _native.call("bsa_sampled_mass_onepass", sq.data_ptr(), sk.data_ptr(), B, H, blocks,
-                     samples, D, bias.data_ptr(), s, 1 if round_bf16 else 0, work.data_ptr(),
-                     nbytes, mass.data_ptr(), _native.err_word(device).data_ptr(),
-                     _stream(device))
+                     samples, D, bias.data_ptr(), s, 1 if round_bf16 else 0,
+                     work.data_ptr() if work is not None else None, nbytes, mass.data_ptr(),
+                     _native.err_word(device).data_ptr(), _stream(device))
         return mass
     _native.call("bsa_sampled_mass", sq.data_ptr(), sk.data_ptr(), B, H, blocks, samples, D,
                  bias.data_ptr(), s, 1 if round_bf16 else 0, mass.data_ptr(),

@@ -212,15 +212,17 @@ BSA_API int bsa_sampled_mass(const void* sampled_q, const void* sampled_k, int64
 
 /*
  * (b) Sampled block mass in one pass over the sampled keys: same inputs,
- * limits and output as bsa_sampled_mass (within float rounding), plus a
- * caller workspace of bsa_sampled_mass_workspace_bytes bytes (16-byte
- * aligned; 1.04 GB for batch 2, 40 heads, 450 blocks, 16 samples).  Each
- * sampled query row writes the log2 of its exponential sum over every key
- * block into the workspace as it streams the keys, with its running
- * stabiliser folded in, and its log-sum-exp at the end; a second kernel then
- * forms mass = mean over the block's query samples of 2^(block - row).  The
- * two-pass entry point computes every score twice instead; samples <= 2
- * (one or two keys per block) take that kernel here too, workspace unused.
+ * limits and output as bsa_sampled_mass (within float rounding).  Each
+ * sampled query row keeps the log2 of its exponential sum over every key
+ * block, with its running stabiliser folded in, as it streams the keys; once
+ * its log-sum-exp is known, mass = mean over the block's query samples of
+ * 2^(block - row).  With 16 or 32 samples and up to 473 blocks those values
+ * stay on chip (TMEM and shared memory): bsa_sampled_mass_workspace_bytes
+ * returns 0 and workspace may be NULL.  Other shapes write them to a caller
+ * workspace of bsa_sampled_mass_workspace_bytes bytes (16-byte aligned) and
+ * a second kernel forms the mass; samples <= 2 (one or two keys per block)
+ * take the two-pass kernel, workspace unused.  The two-pass entry point
+ * computes every score twice instead.
  * Replaces: attention_backends/flex.py:205-251 (_sampled_block_mass).
  */
 BSA_API int64_t bsa_sampled_mass_workspace_bytes(int64_t batch, int64_t heads, int32_t q_blocks,

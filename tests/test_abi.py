@@ -86,10 +86,14 @@ def test_attention_and_mass_validate():
     assert "head_dim" in _err()
     assert lib.bsa_sampled_mass(16, 16, 1, 1, 4, 3, 128, 16, 0.1, 1, 16, 16, None) == -2
     assert "samples" in _err()
-    # one pass: 2 x 40 x 7,200 rows x (450 + 1) floats; a short workspace is refused
-    assert lib.bsa_sampled_mass_workspace_bytes(2, 40, 450, 16) == 2 * 40 * 7200 * 451 * 4
-    assert lib.bsa_sampled_mass_onepass(16, 16, 2, 40, 450, 16, 128, 16, 0.1, 1, 16,
-                                        2 * 40 * 7200 * 451 * 4 - 1, 16, 16, None) == -1
+    # one pass: 16 or 32 samples and up to 473 blocks need no workspace; past
+    # that 2 x 40 x rows x (blocks + 1) floats, and a short workspace is refused
+    assert lib.bsa_sampled_mass_workspace_bytes(2, 40, 450, 16) == 0
+    assert lib.bsa_sampled_mass_workspace_bytes(2, 40, 473, 32) == 0
+    assert lib.bsa_sampled_mass_workspace_bytes(2, 40, 474, 16) == 2 * 40 * 7584 * 475 * 4
+    assert lib.bsa_sampled_mass_workspace_bytes(2, 40, 450, 8) == 2 * 40 * 3600 * 451 * 4
+    assert lib.bsa_sampled_mass_onepass(16, 16, 2, 40, 474, 16, 128, 16, 0.1, 1, 16,
+                                        2 * 40 * 7584 * 475 * 4 - 1, 16, 16, None) == -1
     assert "workspace" in _err()
     assert lib.bsa_exact_block_mass(16, 16, 1, 100, 1, 128, 96, 0.1, None, 16, 16, None) == -2
     assert "block" in _err()

@@ -223,10 +223,14 @@ def test_sampled_mass_480p_matches_reference(golden):
 
 
 @pytest.mark.parametrize("T,block,samples", [(1000, 128, 1), (3000, 128, 2), (4096, 64, 4),
-                                             (2500, 128, 8), (57600, 128, 16), (1900, 64, 32)])
+                                             (2500, 128, 8), (57600, 128, 16), (1900, 64, 32),
+                                             (61000, 128, 16), (5000, 128, 32)])
 def test_sampled_mass_one_pass_matches_two_pass(T, block, samples):
-    """One pass over the sampled keys (per-row block log-sums + reduction)
-    against the two-pass kernel, partial last blocks included; rows sum to 1.
+    """One pass over the sampled keys against the two-pass kernel, partial
+    last blocks included; rows sum to 1.  16 or 32 samples and at most 473
+    blocks keep the per-row block log-sums on chip (no workspace: 57,600 and
+    5,000 tokens); other shapes go through a workspace and a reduction
+    launch (61,000 tokens: 477 blocks).
     Both kernels take a quarter of their exponentials from a polynomial with
     relative error <= 7.5e-5, evaluated at different arguments (running vs
     final stabiliser), hence rtol 2e-4 (the mass parity bound)."""
