@@ -59,6 +59,11 @@ def parse_args(argv=None):
                    help="forward5 only: fewer transformer layers (0 = the model's 40)")
     p.add_argument("--heads", type=int, default=40, help="heads (40 = config 4; fewer for profiling)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cfg-split", action="store_true",
+                   help="one rank group for both CFG branches (every rank exchanges heads)")
+    p.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                   help="N > 2: output exchange by the attention's stores into the ranks' "
+                        "shards over peer memory, or by an NCCL all-to-all")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-route-stage", action="store_true")
     p.add_argument("--no-gpu-comparator", action="store_true",
@@ -453,7 +458,8 @@ def main(argv=None):
     _native.load_library()
 
     cfg = layer_config(args.heads)
-    plan = parallel.make_plan(world, rank, cfg.heads, batch=cfg.batch)
+    plan = parallel.make_plan(world, rank, cfg.heads, batch=cfg.batch,
+                              split_cfg=not args.no_cfg_split)
     group = parallel.new_groups(plan) if world > 1 else None
     branches = plan.branches(cfg.batch)
     hs = plan.head_slice
@@ -485,21 +491,27 @@ def main(argv=None):
         # chunked exchange overlapped with the attention of earlier chunks
         pipe = parallel.PipelinedHeadParallel(group, P, cfg.heads, t_local,
                                               perm=layout.permutation_cpu,
-                                              inverse=layout.inverse_cpu)
+                                              inverse=layout.inverse_cpu,
+                                              peer_out=args.exchange == "peer")
         hc = pipe.hc
         chunk_csr = [(counts[:, c * hc:(c + 1) * hc].contiguous(),
                       indices[:, c * hc:(c + 1) * hc].contiguous()) for c in range(pipe.chunks)]
 
         chunk_events = []
 
-        def attend_chunk(qp, kp, vp, c, out, out_rows):
-            # the output store writes token order straight into the send
-            # buffer of the output all-to-all (the unpack folded in)
+        def attend_chunk(qp, kp, vp, c, out, out_rows, peers=None):
+            # the output store writes token order straight into the ranks'
+            # output shards over peer memory (or into the send buffer of the
+            # output all-to-all): the unpack and the exchange folded in
             cur = torch.cuda.current_stream(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(cur)
-            kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block, out=out,
-                                           out_rows=out_rows)
+            if peers is not None:
+                kernels.block_sparse_attention_peers(qp, kp, vp, *chunk_csr[c], peers,
+                                                     block=cfg.block, out_rows=out_rows)
+            else:
+                kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block,
+                                               out=out, out_rows=out_rows)
             e1.record(cur)
             chunk_events.append((e0, e1))
             if c == pipe.chunks - 1:
@@ -631,8 +643,10 @@ def main(argv=None):
             * cfg.batch / (ms * 1e-3) / 1e12,
             "parallelism": ("single GPU" if world == 1 else
                             f"{plan.cfg_groups} CFG group(s) x {P}-way head parallel "
-                            "(Ulysses all-to-all, NCCL"
-                            + (f", {pipe.chunks} head chunks overlapped with attention)"
+                            "(Ulysses input all-to-all, NCCL"
+                            + (f", {pipe.chunks} head chunks overlapped with attention; output "
+                               + ("stored by the attention into the ranks' shards over peer "
+                                  "memory)" if pipe.peer_out else "all-to-all, NCCL)")
                                if pipe is not None else ")")),
             "l2": "inputs (3 x 1.18 GB) exceed L2; no flush"},
         "stages": stages,

@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -593,7 +594,9 @@ static int attention_launch(const char* name, const void* q, const void* k, cons
                             int32_t route_has_batch, int32_t block, float scale, void* out,
                             int64_t out_stride_b, int64_t out_stride_t, int64_t out_stride_h,
                             float* lse, float* block_lse, int32_t* err_word, void* stream,
-                            const int32_t* out_rows = nullptr) {
+                            const int32_t* out_rows = nullptr,
+                            const void* const* out_peers = nullptr, int32_t n_peers = 0,
+                            int64_t peer_tokens = 0) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || counts == nullptr ||
       indices == nullptr || err_word == nullptr)
     return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
@@ -646,6 +649,10 @@ static int attention_launch(const char* name, const void* q, const void* k, cons
   a.err_word = err_word;
   a.block_lse = block_lse;
   a.out_rows = out_rows;
+  a.n_peer = n_peers;
+  a.peer_tokens = peer_tokens;
+  for (int d = 0; d < n_peers; ++d)
+    a.out_peer[d] = static_cast<__nv_bfloat16*>(const_cast<void*>(out_peers[d]));
   cudaError_t e = bsa::launch_attention(tq, tk, tv, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, name);
   return ok();
@@ -661,6 +668,84 @@ int bsa_attention_fwd(const void* q, const void* k, const void* v, int64_t batch
                           in_stride_b, in_stride_t, in_stride_h, counts, indices, route_cols,
                           route_has_batch, block, scale, out, out_stride_b, out_stride_t,
                           out_stride_h, lse, nullptr, err_word, stream);
+}
+
+int bsa_attention_fwd_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                            int64_t heads, int32_t head_dim, int64_t in_stride_t,
+                            int64_t in_stride_h, const int32_t* counts, const int32_t* indices,
+                            int32_t route_cols, int32_t block, float scale,
+                            const int32_t* out_rows, const void* const* out_peers,
+                            int32_t n_peers, int64_t peer_tokens, int64_t out_stride_t,
+                            int64_t out_stride_h, int32_t* err_word, void* stream) {
+  if (out_peers == nullptr || n_peers < 1 || n_peers > bsa::kMaxPeers)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "1 to %d output peers needed (got %d)", bsa::kMaxPeers,
+                n_peers);
+  if (peer_tokens <= 0 || peer_tokens * n_peers != tokens)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "peers x peer_tokens must equal tokens");
+  for (int d = 0; d < n_peers; ++d) {
+    if (out_peers[d] == nullptr || (reinterpret_cast<uintptr_t>(out_peers[d]) & 15))
+      return fail(BSA_ERR_INVALID_ARGUMENT, "output peer %d is null or not 16-byte aligned", d);
+    if (out_peers[d] == q || out_peers[d] == k || out_peers[d] == v)
+      return fail(BSA_ERR_INVALID_ARGUMENT, "output peers must not alias q, k or v");
+  }
+  return attention_launch("bsa_attention_fwd_peers launch", q, k, v, 1, tokens, heads, head_dim,
+                          tokens * in_stride_t, in_stride_t, in_stride_h, counts, indices,
+                          route_cols, 0, block, scale, const_cast<void*>(out_peers[0]), 0,
+                          out_stride_t, out_stride_h, nullptr, nullptr, err_word, stream, out_rows,
+                          out_peers, n_peers, peer_tokens);
+}
+
+// CUDA IPC of device buffers between the processes of a head-parallel group.
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
+
+int bsa_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  AddressRangeFn range = address_range_fn();
+  if (range == nullptr) return fail(BSA_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(BSA_ERR_CUDA, "cuMemGetAddressRange failed (%d)", (int)r);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_ipc_export");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return ok();
+}
+
+int bsa_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  if (handle == nullptr || ptr == nullptr || offset < 0)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_ipc_import");
+  *ptr = static_cast<char*>(base) + offset;
+  return ok();
+}
+
+int bsa_ipc_release(void* ptr, int64_t offset) {
+  if (ptr == nullptr || offset < 0) return fail(BSA_ERR_INVALID_ARGUMENT, "bad argument");
+  const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_ipc_release");
+  return ok();
 }
 
 int bsa_attention_fwd_scatter(const void* q, const void* k, const void* v, int64_t batch,

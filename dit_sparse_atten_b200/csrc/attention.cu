@@ -435,9 +435,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         row_store = false;
       }
     }
+    // Multi-GPU: the row's token lives on rank out_token / peer_tokens, whose
+    // output shard is mapped into this process (the stores cross NVLink).
+    __nv_bfloat16* out_base = a.out + b * a.out_stride_b;
+    if (a.n_peer > 0 && row_store) {
+      const int64_t d = out_token / a.peer_tokens;
+      if (d >= a.n_peer) {
+        atomicOr(a.err_word, kErrBadRoute);
+        row_store = false;
+      } else {
+        out_base = a.out_peer[d];
+        out_token -= d * a.peer_tokens;
+      }
+    }
     if (warp_active && grp < 2) {
-      __nv_bfloat16* out = a.out + b * a.out_stride_b + out_token * a.out_stride_t +
-                           h * a.out_stride_h + grp * 64;
+      __nv_bfloat16* out = out_base + out_token * a.out_stride_t + h * a.out_stride_h + grp * 64;
       const float inv_l = (n > 0 && l_row > 0.f) ? 1.f / l_row : 0.f;
 #pragma unroll 1
       for (int cc = 0; cc < kHeadDim / 64; ++cc) {
@@ -466,6 +478,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
+      // Peer stores are ordered before whatever this thread does next at
+      // system scope (the host then joins the ranks with a collective).
+      if (a.n_peer > 0) __threadfence_system();
       if (row_valid && grp == 0 && a.lse != nullptr) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
             (n > 0 && l_row > 0.f) ? (m_fin + __log2f(l_row)) * kLn2 : -INFINITY;
@@ -569,7 +584,10 @@ cudaError_t launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const
     const char* v = getenv("BSA_ATTENTION_KERNEL");
     return v != nullptr && strcmp(v, "pair") == 0;
   }();
-  if (a.block == 128 && pair) return launch_attention_pair(tq, tk, tv, a, stream);
+  if (a.n_peer > 0 && (a.batch != 1 || a.block_lse != nullptr || a.peer_tokens <= 0 ||
+                      a.n_peer > kMaxPeers))
+    return cudaErrorInvalidValue;
+  if (a.block == 128 && pair && a.n_peer == 0) return launch_attention_pair(tq, tk, tv, a, stream);
   if (a.block_lse != nullptr) {
     if (a.block == 128) return launch_bk<128, true>(tq, tk, tv, a, stream);
     return cudaErrorInvalidValue;

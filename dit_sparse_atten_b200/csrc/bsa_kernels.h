@@ -139,6 +139,8 @@ cudaError_t launch_gather_samples(const void* q, const void* k, int64_t T, int64
                                   cudaStream_t stream);
 
 // ---- (a) block-sparse attention --------------------------------------------
+constexpr int kMaxPeers = 8;   // ranks of one head-parallel group the attention stores to
+
 struct AttnArgs {
   int64_t batch, tokens, heads;
   int32_t q_blocks, k_blocks;     // ceil(T / block)
@@ -162,6 +164,13 @@ struct AttnArgs {
   // order (counts / indices unused) and receives [B, H, Kb, T] per-row,
   // per-key-block log2 exponential sums (block == 128).
   float* block_lse;
+  // Output shards on the ranks of a head-parallel group (batch 1): with
+  // n_peer > 0 the row of token t goes to rank d = t / peer_tokens, token
+  // t - d * peer_tokens of out_peer[d] (out_stride_t / out_stride_h apply),
+  // out_peer[d] being rank d's buffer mapped into this process.  out unused.
+  int32_t n_peer;
+  int64_t peer_tokens;
+  __nv_bfloat16* out_peer[kMaxPeers];
 };
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args,

@@ -365,6 +365,9 @@ class FlexReuseBackend:
         self.route_streams = {}
         self.spatial_layouts = {}
         self.pipelines = {}
+        # head_parallel on CUDA: the attention stores into the ranks' output
+        # shards over peer memory instead of an output all-to-all
+        self.peer_exchange = True
         self.log = PhaseLog()
 
     @property
@@ -716,8 +719,9 @@ class FlexReuseBackend:
         exchanges the heads in chunks overlapped with the attention
         (``parallel.PipelinedHeadParallel``): chunk c's heads attend over
         their slice of the layer's CSR route, packed by the exchange's row
-        gather and stored back to token order into the output exchange's send
-        buffer.  Every other call (bootstrap, refreshes, updates, dense
+        gather, and the kernel stores each output row into the output shard
+        of the rank that holds its token (peer memory; ``peer_exchange``
+        False: into the send buffer of an output all-to-all).  Every other call (bootstrap, refreshes, updates, dense
         dispatch, non-default arguments) exchanges all heads at once
         (``parallel.head_parallel_attention``) and runs ``__call__``.
         ``call_kw`` are ``__call__``'s keyword arguments.
@@ -739,14 +743,20 @@ class FlexReuseBackend:
             perm = layout.permutation_cpu if layout is not None else None
             inverse = layout.inverse_cpu if layout is not None else None
             pipe = parallel.PipelinedHeadParallel(group, group_size, heads, q.shape[1], perm,
-                                                  inverse, chunks=chunks, rows=rows)
+                                                  inverse, chunks=chunks, rows=rows,
+                                                  peer_out=self.peer_exchange and q.is_cuda)
             self.pipelines[pkey] = pipe
         counts, indices = state.block_mask.counts[0], state.block_mask.indices[0]
         hc = pipe.hc
         scale = call_kw.get("softmax_scale")
 
-        def attend(qp, kp, vp, chunk, out, out_rows):
+        def attend(qp, kp, vp, chunk, out, out_rows, peers=None):
             hs = slice(chunk * hc, (chunk + 1) * hc)
+            if peers is not None:
+                kernels.block_sparse_attention_peers(qp, kp, vp, counts[hs], indices[hs], peers,
+                                                     block=self.config.block_size, scale=scale,
+                                                     out_rows=out_rows)
+                return
             kernels.block_sparse_attention(qp, kp, vp, counts[hs], indices[hs],
                                            block=self.config.block_size, scale=scale, out=out,
                                            out_rows=out_rows)

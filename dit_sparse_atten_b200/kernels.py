@@ -556,3 +556,82 @@ def block_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                  _native.ptr(lse), _native.err_word(device).data_ptr(), _stream(device))
     return (out, lse) if return_lse else out
 
+
+
+def block_sparse_attention_peers(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                 counts: torch.Tensor, indices: torch.Tensor,
+                                 peers: "PeerRows", block: int = 128,
+                                 scale: float | None = None,
+                                 out_rows: torch.Tensor | None = None) -> None:
+    """Block-sparse attention of one branch (``[1, T, H, D]``) whose output
+    rows go straight to the ranks holding their tokens (``bsa_attention_fwd_peers``):
+    token ``t = out_rows[i]`` of packed row i lands in rank ``t // peers.tokens``'s
+    buffer ``peers.ptrs[d]`` (strides ``peers.stride_t``, ``peers.stride_h``
+    elements, this call's head h at ``h * stride_h``).  ``counts [H, Qb]``,
+    ``indices [H, Qb, >= Qb]`` int32."""
+    device = _require_cuda(q, k, v, counts, indices)
+    if not (q.shape == k.shape == v.shape) or q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("q, k and v must be [1, T, H, D] with equal shapes")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("block_sparse_attention_peers expects bf16 q, k, v")
+    _, T, H, D = q.shape
+    if D != HEAD_DIM:
+        raise NotImplementedError(f"head_dim must be {HEAD_DIM}")
+    blocks = math.ceil(T / block)
+    if tuple(counts.shape) != (H, blocks) or tuple(indices.shape[:-1]) != (H, blocks):
+        raise ValueError("counts must be [H, Qb] and indices [H, Qb, route_cols]")
+    if counts.dtype != torch.int32 or indices.dtype != torch.int32:
+        raise ValueError("counts and indices must be int32")
+    if out_rows is not None and (out_rows.dtype != torch.int32 or out_rows.shape != (T,)
+                                 or out_rows.device != q.device):
+        raise ValueError("out_rows must be int32 [T] on q's device")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    counts, indices = counts.contiguous(), indices.contiguous()
+    arr = (ctypes.c_void_p * len(peers.ptrs))(*peers.ptrs)
+    s = float(scale) if scale is not None else D ** -0.5
+    _native.call("bsa_attention_fwd_peers", q.data_ptr(), k.data_ptr(), v.data_ptr(), T, H, D,
+                 q.stride(1), q.stride(2), counts.data_ptr(), indices.data_ptr(),
+                 indices.shape[-1], block, s, _native.ptr(out_rows), arr, len(peers.ptrs),
+                 peers.tokens, peers.stride_t, peers.stride_h,
+                 _native.err_word(device).data_ptr(), _stream(device))
+
+
+class PeerRows:
+    """Destinations of a head-parallel output: ``ptrs[d]`` is rank d's output
+    shard (mapped into this process), at this call's first head; ``tokens``
+    tokens per rank; element strides ``stride_t``, ``stride_h``."""
+
+    def __init__(self, ptrs, tokens, stride_t, stride_h):
+        self.ptrs = [int(p) for p in ptrs]
+        self.tokens = int(tokens)
+        self.stride_t = int(stride_t)
+        self.stride_h = int(stride_h)
+
+    def shifted(self, heads: int, elem_bytes: int = 2) -> "PeerRows":
+        """The same destinations ``heads`` heads further on."""
+        off = heads * self.stride_h * elem_bytes
+        return PeerRows([p + off for p in self.ptrs], self.tokens, self.stride_t, self.stride_h)
+
+
+def ipc_export(t: torch.Tensor):
+    """(64-byte CUDA IPC handle of ``t``'s allocation, ``t``'s byte offset in it)."""
+    _require_cuda(t)
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_int64(0)
+    _native.call("bsa_ipc_export", t.data_ptr(), handle, ctypes.byref(offset))
+    return bytes(handle.raw), int(offset.value)
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Map another process's allocation on the current device; returns the
+    device pointer at ``offset``."""
+    if len(handle) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    buf = ctypes.create_string_buffer(handle, 64)
+    out = ctypes.c_void_p(0)
+    _native.call("bsa_ipc_import", buf, int(offset), ctypes.byref(out))
+    return int(out.value)
+
+
+def ipc_release(ptr: int, offset: int) -> None:
+    _native.call("bsa_ipc_release", int(ptr), int(offset))

@@ -192,6 +192,55 @@ def head_parallel_attention(q, k, v, attend, group, group_size, rows=None):
     return out
 
 
+# Allocations of other processes mapped into this one, by IPC handle: a
+# handle (one cudaMalloc segment) is opened once per process and reused.
+_IPC_BASES: dict = {}
+
+
+class PeerShards:
+    """This rank's output shard ``[T/P, H, D]`` and every group rank's shard
+    mapped into this process (CUDA IPC, exchanged once over the group), so an
+    attention kernel can store each output row into the rank that holds its
+    token.  ``ptrs[d]`` is rank d's shard (this rank's own for d = its rank)."""
+
+    def __init__(self, group, group_size, shape, dtype, device):
+        from . import kernels
+        self.local = torch.empty(shape, dtype=dtype, device=device)
+        self.ptrs = []
+        self.error = None
+        try:
+            handle, offset = kernels.ipc_export(self.local)
+        except RuntimeError as exc:          # e.g. memory the runtime cannot export
+            self.error = exc
+            handle, offset = bytes(64), 0
+        mine = torch.tensor(list(handle) + list(int(offset).to_bytes(8, "little")),
+                            dtype=torch.uint8, device=device)
+        every = [torch.empty_like(mine) for _ in range(group_size)]
+        dist.all_gather(every, mine, group=group)
+        me = dist.get_rank(group)
+        for r, t in enumerate(every):
+            if self.error is not None:
+                break
+            if r == me:
+                self.ptrs.append(self.local.data_ptr())
+                continue
+            raw = bytes(t.cpu().tolist())
+            off = int.from_bytes(raw[64:], "little")
+            base = _IPC_BASES.get(raw[:64])
+            try:
+                if base is None:
+                    base = kernels.ipc_import(raw[:64], 0)
+                    _IPC_BASES[raw[:64]] = base
+            except RuntimeError as exc:
+                self.error = exc
+                break
+            self.ptrs.append(base + off)
+        # every rank takes the same exchange: peer stores only if all mapped
+        ok = torch.tensor([0 if self.error is not None else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        self.ready = bool(ok.item())
+
+
 def pipeline_chunks(heads_per_rank):
     """Head chunks per rank for ``PipelinedHeadParallel``: 4, 2, 5 or 3 chunks
     of at least 4 heads each, else 1.  Smaller chunks hide more of the
@@ -225,10 +274,20 @@ class PipelinedHeadParallel:
     ``out`` (``[1, T, hc, D]``; ``out_rows`` is None without a permutation) and
     returns None - the block-sparse kernel's folded unpack - or returns the
     output in pack order.  ``rows`` supplies the row moves (``CudaRows``).
+
+    ``peer_out`` (CUDA): no output all-to-all.  Every rank's output shard is
+    mapped into the others (``PeerShards``) and ``attend`` is called with
+    ``out=None`` and ``peers=`` a ``kernels.PeerRows`` for the chunk's heads:
+    the attention kernel stores each row into the rank holding its token
+    (``kernels.block_sparse_attention_peers``), so the output exchange runs
+    inside the attention.  One small all-reduce then joins the ranks before
+    the shard is read.  The next call's first input exchange cannot complete
+    before every rank has started that call, so no rank stores into a shard
+    its owner is still reading.
     """
 
     def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
-                 chunks=None, rows=None):
+                 chunks=None, rows=None, peer_out=False):
         if heads % group_size:
             raise ValueError(f"{heads} heads do not split over {group_size} ranks")
         self.group = group
@@ -261,6 +320,9 @@ class PipelinedHeadParallel:
             builders["inverse"] = lambda: inv
         self.tables = _Tables(builders)
         self.rows = rows or CudaRows
+        self.peer_out = peer_out
+        self.peer_error = None
+        self._shards = {}
 
     def __call__(self, q, k, v, attend):
         b, tl, h, d = q.shape
@@ -280,10 +342,14 @@ class PipelinedHeadParallel:
             inputs.append(dist.all_to_all_single(recv[c], send[c], group=self.group,
                                                  async_op=True))
         span = (3 * P - 2) * tl
+        out_rows = tab("perm") if self.has_perm else None
+        if self.peer_out:
+            out = self._peer_call(q, recv, inputs, attend, out_rows, span)
+            if out is not None:
+                return out
         out_send = torch.empty((C, T, hc, d), dtype=q.dtype, device=dev)
         orecv = torch.empty_like(out_send)
         outputs = []
-        out_rows = tab("perm") if self.has_perm else None
         for c in range(C):
             inputs[c].wait()
             r = recv[c][None]
@@ -304,6 +370,32 @@ class PipelinedHeadParallel:
             outputs[c].wait()
             self.rows.scatter([orecv[c][None]], [dst], tab("out_src"), tab(f"send_src{c}"))
         return out
+
+    def _peer_call(self, q, recv, inputs, attend, out_rows, span):
+        from .kernels import PeerRows
+        _, tl, h, d = q.shape
+        key = (q.device, q.dtype)
+        shards = self._shards.get(key)
+        if shards is None:
+            shards = self._shards[key] = PeerShards(self.group, self.P, (tl, h, d), q.dtype,
+                                                    q.device)
+        if not shards.ready:
+            # some rank could not map the shards: every rank exchanges by NCCL
+            self.peer_out = False
+            self.peer_error = shards.error
+            return None
+        me = dist.get_rank(self.group)
+        mine = PeerRows(shards.ptrs, tl, h * d, d).shifted(me * self.hp)
+        for c in range(self.chunks):
+            inputs[c].wait()
+            r = recv[c][None]
+            qp, kp, vp = self.rows.gather([r[:, t * tl:t * tl + span] for t in range(3)],
+                                          self.tables.get("recv_perm", q.device))
+            attend(qp, kp, vp, c, None, out_rows, peers=mine.shifted(c * self.hc))
+        # every rank's stores into this shard are done once all ranks get here
+        joined = torch.zeros(1, dtype=torch.float32, device=q.device)
+        dist.all_reduce(joined, group=self.group)
+        return shards.local.clone().view(1, tl, h, d)
 
 
 def all_reduce_count(count, group=None):

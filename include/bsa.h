@@ -319,12 +319,45 @@ BSA_API int bsa_attention_fwd_scatter(const void* q, const void* k, const void* 
                                       int32_t* err_word, void* stream);
 
 /*
- * Diagnostics: y[i] = 2^x[i] for n float32 values through one of the two
- * exponential paths of the softmax kernels: mode 0 = the MUFU ex2.approx
- * instruction, mode 1 = the FMA-pipe polynomial (Cody-Waite split + Remez
- * degree-3, relative error <= 1e-4 for x >= -126).  No reference
- * counterpart: it exists so the approximation can be tested on its own.
+ * (a) + (e) Block-sparse attention of one CFG branch (batch 1) of a
+ * head-parallel group, storing every output row straight into the output
+ * shard of the rank that holds its token: packed row i is token
+ * t = out_rows[i] (out_rows may be NULL: t = i), which belongs to rank
+ * d = t / peer_tokens and is written to token t - d * peer_tokens of
+ * out_peers[d] with strides (out_stride_t, out_stride_h) elements, head h of
+ * this call at out_peers[d] + h * out_stride_h.  out_peers[d] is rank d's
+ * buffer mapped into this process (bsa_ipc_import; this rank's own buffer
+ * for d = its rank), n_peers * peer_tokens == tokens, n_peers <= 8.  The
+ * stores cross NVLink while the kernel runs: the attention and the output
+ * all-to-all of the Ulysses exchange are one kernel.  The caller joins the
+ * ranks (a collective on the stream) before reading its shard.  q, k, v:
+ * [tokens, heads, head_dim] with the given strides; route as
+ * bsa_attention_fwd (one route for the batch).
+ * Replaces: attention_backends/flex.py:358-399 (_flex_output) and the
+ * restore of flex.py:694-700, on a head shard; the exchange has no
+ * counterpart (the reference runs on one device).
  */
+BSA_API int bsa_attention_fwd_peers(const void* q, const void* k, const void* v, int64_t tokens,
+                                    int64_t heads, int32_t head_dim, int64_t in_stride_t,
+                                    int64_t in_stride_h, const int32_t* counts,
+                                    const int32_t* indices, int32_t route_cols, int32_t block,
+                                    float scale, const int32_t* out_rows,
+                                    const void* const* out_peers, int32_t n_peers,
+                                    int64_t peer_tokens, int64_t out_stride_t,
+                                    int64_t out_stride_h, int32_t* err_word, void* stream);
+
+/*
+ * (e) CUDA IPC of a device buffer between the processes of a head-parallel
+ * group.  bsa_ipc_export writes the 64-byte handle of the allocation holding
+ * ptr and ptr's offset in it; bsa_ipc_import maps a handle exported by
+ * another process into this process on the current device (peer access
+ * enabled) and returns the pointer at offset; bsa_ipc_release unmaps it
+ * (ptr and offset as returned / given).  No reference counterpart.
+ */
+BSA_API int bsa_ipc_export(const void* ptr, void* handle, int64_t* offset);
+BSA_API int bsa_ipc_import(const void* handle, int64_t offset, void** ptr);
+BSA_API int bsa_ipc_release(void* ptr, int64_t offset);
+
 /*
  * (a) + (f1) Dense attention with its exact block mass, one attention pass:
  * out = softmax(q k^T * scale) v over all keys, lse = its natural-log

@@ -2,7 +2,8 @@
 
 Two ranks hold sequence shards of one branch; every exchange path - the
 unchunked ``head_parallel_attention``, the chunked ``PipelinedHeadParallel``
-with the routed kernel storing into the output all-to-all's send buffer, and
+with the routed kernel storing into the output all-to-all's send buffer or
+straight into the ranks' output shards over peer memory (twice in a row), and
 the public ``FlexReuseBackend.head_parallel`` on a reuse call - must give the
 single-GPU result on every row of the rank's shard.  Skipped with fewer than two GPUs; the host-side
 layout logic is covered on CPU by tests/test_parallel_gloo.py.
@@ -71,13 +72,28 @@ def _worker(rank, world, port, queue):
                                               chunks=2)
         hc = pipe.hc
 
-        def attend_chunk(qp_, kp_, vp_, c, out_c, out_rows):
+        def attend_chunk(qp_, kp_, vp_, c, out_c, out_rows, peers=None):
             cs = slice(c * hc, (c + 1) * hc)
+            if peers is not None:
+                kernels.block_sparse_attention_peers(qp_, kp_, vp_, c_loc[cs].contiguous(),
+                                                     i_loc[cs].contiguous(), peers,
+                                                     out_rows=out_rows)
+                return
             kernels.block_sparse_attention(qp_, kp_, vp_, c_loc[cs].contiguous(),
                                            i_loc[cs].contiguous(), out=out_c, out_rows=out_rows)
 
         out2 = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
                     attend_chunk)
+        # the output exchange inside the attention: stores into the ranks'
+        # shards over peer memory, twice in a row (the second call stores into
+        # shards the first call's owners have read)
+        pipe_p = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
+                                                perm=lay.permutation_cpu,
+                                                inverse=lay.inverse_cpu, chunks=2, peer_out=True)
+        shard = [x[:, sl].contiguous() for x in (q, k, v)]
+        out4 = pipe_p(*shard, attend_chunk)
+        out5 = pipe_p(*[x.flip(1).contiguous() for x in shard], attend_chunk)
+        out4b = pipe_p(*shard, attend_chunk)
         # the public API: FlexReuseBackend.head_parallel on a reuse call
         backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True))
         backend.install_route(route[hs].to(dev), attention_id=1, branch=0, tokens=T, heads=hp,
@@ -90,6 +106,10 @@ def _worker(rank, world, port, queue):
         assert backend.pipelines and backend.phase_counts["sparse_reuse"] == 1
         errs.append(float((out2.float() - ref[:, sl].float()).abs().max()))
         errs.append(float((out3.float() - ref[:, sl].float()).abs().max()))
+        errs.append(float((out4.float() - ref[:, sl].float()).abs().max()))
+        errs.append(float((out4b.float() - ref[:, sl].float()).abs().max()))
+        assert not torch.equal(out5, out4)
+        assert backend.pipelines and all(p.peer_out for p in backend.pipelines.values())
         queue.put((rank, errs))
     except Exception as exc:
         queue.put((rank, repr(exc)))
@@ -112,4 +132,4 @@ def test_exchange_paths_match_single_gpu():
     for rank, errs in results.items():
         assert not isinstance(errs, str), errs
         # the same kernels on the same rows: the exchange must not change a bit
-        assert errs == [0.0, 0.0, 0.0], (rank, errs)
+        assert errs == [0.0] * 5, (rank, errs)
