@@ -487,15 +487,18 @@ def main(argv=None):
     stream = torch.cuda.current_stream(device)
     attn_events = []
     pipe = None
-    if P > 1 and len(branches) == 1:
-        # chunked exchange overlapped with the attention of earlier chunks
+    if P > 1:
+        # chunked exchange overlapped with the attention of earlier chunks,
+        # one pipelined call per CFG branch of this rank's group
         pipe = parallel.PipelinedHeadParallel(group, P, cfg.heads, t_local,
                                               perm=layout.permutation_cpu,
                                               inverse=layout.inverse_cpu,
                                               peer_out=args.exchange == "peer")
         hc = pipe.hc
-        chunk_csr = [(counts[:, c * hc:(c + 1) * hc].contiguous(),
-                      indices[:, c * hc:(c + 1) * hc].contiguous()) for c in range(pipe.chunks)]
+        chunk_csr = [[(counts[bi, c * hc:(c + 1) * hc].contiguous(),
+                       indices[bi, c * hc:(c + 1) * hc].contiguous())
+                      for c in range(pipe.chunks)] for bi in range(len(branches))]
+        branch_now = [0]
 
         chunk_events = []
 
@@ -506,12 +509,13 @@ def main(argv=None):
             cur = torch.cuda.current_stream(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(cur)
+            csr = chunk_csr[branch_now[0]][c]
             if peers is not None:
-                kernels.block_sparse_attention_peers(qp, kp, vp, *chunk_csr[c], peers,
-                                                     block=cfg.block, out_rows=out_rows)
+                kernels.block_sparse_attention_peers(qp, kp, vp, *csr, peers, block=cfg.block,
+                                                     out_rows=out_rows)
             else:
-                kernels.block_sparse_attention(qp, kp, vp, *chunk_csr[c], block=cfg.block,
-                                               out=out, out_rows=out_rows)
+                kernels.block_sparse_attention(qp, kp, vp, *csr, block=cfg.block, out=out,
+                                               out_rows=out_rows)
             e1.record(cur)
             chunk_events.append((e0, e1))
             if c == pipe.chunks - 1:
@@ -536,9 +540,11 @@ def main(argv=None):
 
     def step():
         if pipe is not None:
-            return pipe(q, k, v, attend_chunk)
-        if P > 1:
-            return parallel.head_parallel_attention(q, k, v, attend, group, P)
+            outs = []
+            for bi in range(len(branches)):
+                branch_now[0] = bi
+                outs.append(pipe(q[bi:bi + 1], k[bi:bi + 1], v[bi:bi + 1], attend_chunk))
+            return outs
         return attend(q, k, v)
 
     def barrier():
@@ -655,7 +661,11 @@ def main(argv=None):
         # pack + attention per step (unpack folded into the store); the chunked
         # exchange runs send gather, packed gather, attention and output
         # scatter per chunk
-        "gpu_launches": args.steps * world * (4 * pipe.chunks if pipe is not None else 2),
+        # per rank and branch: C send-row scatters, C receive gathers, C
+        # attentions (+ C output scatters with the NCCL output all-to-all)
+        "gpu_launches": args.steps * world * (
+            len(branches) * pipe.chunks * (3 if pipe.peer_out else 4) if pipe is not None
+            else 2),
         **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),
     }

@@ -436,7 +436,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     // Multi-GPU: the row's token lives on rank out_token / peer_tokens, whose
-    // output shard is mapped into this process (the stores cross NVLink).
+    // output shard is mapped into this process (the stores cross NVLink; they
+    // are complete when the kernel is, and the host joins the ranks with a
+    // collective after it before any shard is read).
     __nv_bfloat16* out_base = a.out + b * a.out_stride_b;
     if (a.n_peer > 0 && row_store) {
       const int64_t d = out_token / a.peer_tokens;
@@ -478,9 +480,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
-      // Peer stores are ordered before whatever this thread does next at
-      // system scope (the host then joins the ranks with a collective).
-      if (a.n_peer > 0) __threadfence_system();
       if (row_valid && grp == 0 && a.lse != nullptr) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.tokens + token] =
             (n > 0 && l_row > 0.f) ? (m_fin + __log2f(l_row)) * kLn2 : -INFINITY;

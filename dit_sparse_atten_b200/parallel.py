@@ -60,14 +60,28 @@ def make_plan(world, rank, heads, batch=2, split_cfg=True):
                         rank % group_size, heads)
 
 
+def exchange_group_options():
+    """Process-group options for the head exchange: on NCCL, collectives on
+    high-priority streams.  The attention fills every SM (one CTA per SM),
+    so a collective issued under it gets SMs only as its CTAs retire; with
+    higher priority the collective's CTAs take the next free SMs instead of
+    waiting for the whole attention grid, and the exchange of chunk c + 1
+    runs under chunk c's attention."""
+    if dist.get_backend() != "nccl":
+        return None
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    return opts
+
+
 def new_groups(plan):
-    """Create the CFG rank groups (every rank calls this with the same plan)."""
-    if plan.cfg_groups == 1:
-        return dist.group.WORLD
+    """Create the exchange groups, one per CFG branch group (every rank calls
+    this with the same plan); NCCL groups run on high-priority streams."""
+    opts = exchange_group_options()
     mine = None
     for g in range(plan.cfg_groups):
         ranks = list(range(g * plan.group_size, (g + 1) * plan.group_size))
-        pg = dist.new_group(ranks)
+        pg = dist.new_group(ranks, pg_options=opts)
         if g == plan.group_index:
             mine = pg
     return mine
