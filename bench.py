@@ -62,8 +62,9 @@ def parse_args(argv=None):
     p.add_argument("--no-cfg-split", action="store_true",
                    help="one rank group for both CFG branches (every rank exchanges heads)")
     p.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
-                   help="N > 2: output exchange by the attention's stores into the ranks' "
-                        "shards over peer memory, or by an NCCL all-to-all")
+                   help="N > 2: head exchange over peer memory (inputs pulled from the ranks' "
+                        "shards, outputs stored by the attention into them), or by NCCL "
+                        "all-to-alls")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-route-stage", action="store_true")
     p.add_argument("--no-gpu-comparator", action="store_true",
@@ -493,8 +494,16 @@ def main(argv=None):
         pipe = parallel.PipelinedHeadParallel(group, P, cfg.heads, t_local,
                                               perm=layout.permutation_cpu,
                                               inverse=layout.inverse_cpu,
-                                              peer_out=args.exchange == "peer")
+                                              peer_out=args.exchange == "peer",
+                                              peer_in=args.exchange == "peer")
         hc = pipe.hc
+        if pipe.peer_in and len(branches) == 1:
+            # the step's inputs live in this rank's mapped input shard (as a
+            # caller that produces them there would have them): no copy
+            bufs = pipe.input_buffers(device, q.dtype, cfg.head_dim)
+            for dst_t, src_t in zip(bufs, (q, k, v)):
+                dst_t.copy_(src_t)
+            q, k, v = bufs
         chunk_csr = [[(counts[bi, c * hc:(c + 1) * hc].contiguous(),
                        indices[bi, c * hc:(c + 1) * hc].contiguous())
                       for c in range(pipe.chunks)] for bi in range(len(branches))]
@@ -649,11 +658,12 @@ def main(argv=None):
             * cfg.batch / (ms * 1e-3) / 1e12,
             "parallelism": ("single GPU" if world == 1 else
                             f"{plan.cfg_groups} CFG group(s) x {P}-way head parallel "
-                            "(Ulysses input all-to-all, NCCL"
-                            + (f", {pipe.chunks} head chunks overlapped with attention; output "
-                               + ("stored by the attention into the ranks' shards over peer "
-                                  "memory)" if pipe.peer_out else "all-to-all, NCCL)")
-                               if pipe is not None else ")")),
+                            + (f"({pipe.chunks} head chunks overlapped with attention; "
+                               + ("inputs pulled from the ranks' shards and outputs stored by "
+                                  "the attention into them, over peer memory)"
+                                  if pipe.peer_in else
+                                  "NCCL input and output all-to-alls)")
+                               if pipe is not None else "(NCCL)")),
             "l2": "inputs (3 x 1.18 GB) exceed L2; no flush"},
         "stages": stages,
         **({"gpu_comparator": comparator} if comparator is not None else {}),
@@ -664,8 +674,8 @@ def main(argv=None):
         # per rank and branch: C send-row scatters, C receive gathers, C
         # attentions (+ C output scatters with the NCCL output all-to-all)
         "gpu_launches": args.steps * world * (
-            len(branches) * pipe.chunks * (3 if pipe.peer_out else 4) if pipe is not None
-            else 2),
+            len(branches) * pipe.chunks * (2 if pipe.peer_in else 3 if pipe.peer_out else 4)
+            if pipe is not None else 2),
         **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),
     }

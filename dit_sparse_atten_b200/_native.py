@@ -49,6 +49,7 @@ SIGNATURES = {
                                         _F32, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P], _I32),
     "bsa_attention_fwd_peers": ([_P, _P, _P, _I64, _I64, _I32, _I64, _I64, _P, _P, _I32, _I32,
                                  _F32, _P, _P, _I32, _I64, _I64, _I64, _P, _P], _I32),
+    "bsa_pull_rows": ([_P, _I32, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P], _I32),
     "bsa_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_int64)], _I32),
     "bsa_ipc_import": ([_P, _I64, ctypes.POINTER(ctypes.c_void_p)], _I32),
     "bsa_ipc_release": ([_P, _I64], _I32),

@@ -695,6 +695,29 @@ int bsa_attention_fwd_peers(const void* q, const void* k, const void* v, int64_t
                           out_peers, n_peers, peer_tokens);
 }
 
+int bsa_pull_rows(const void* const* peer_shards, int32_t n_peers, int64_t peer_tokens,
+                  int64_t src_row_bytes, int64_t src_tensor_bytes, int64_t src_offset,
+                  const int32_t* perm, int64_t tokens, int64_t row_bytes, void* const* dst,
+                  int32_t* err_word, void* stream) {
+  if (peer_shards == nullptr || dst == nullptr || err_word == nullptr)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n_peers < 1 || n_peers > bsa::kMaxPeers)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "1 to %d peers needed (got %d)", bsa::kMaxPeers,
+                n_peers);
+  if (peer_tokens <= 0 || peer_tokens * n_peers != tokens)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "peers x peer_tokens must equal tokens");
+  if (row_bytes <= 0 || (row_bytes & 15) || (src_row_bytes & 15) || (src_tensor_bytes & 15) ||
+      (src_offset & 15) || src_offset + row_bytes > src_row_bytes)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "row sizes and offsets must be 16-byte multiples "
+                "and the pulled bytes must lie inside a token's row");
+  cudaError_t e = bsa::launch_pull_rows(peer_shards, n_peers, peer_tokens, src_row_bytes,
+                                        src_tensor_bytes, src_offset, perm, tokens, row_bytes,
+                                        dst, err_word, static_cast<cudaStream_t>(stream),
+                                        sm_count());
+  if (e != cudaSuccess) return cuda_fail(e, "bsa_pull_rows launch");
+  return ok();
+}
+
 // CUDA IPC of device buffers between the processes of a head-parallel group.
 typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
 

@@ -17,6 +17,13 @@ cudaError_t launch_reorder_rows(int n_tensors, const void* const* src, void* con
                                 int64_t tokens_in, int64_t row_bytes, int* err_word,
                                 cudaStream_t stream, int num_sms,
                                 const int32_t* dst_rows = nullptr, int64_t tokens_dst = 0);
+// Head-parallel input exchange: packed rows of this call's heads pulled from
+// the ranks' input shards (peer memory) into dst[0..2] (reorder.cu).
+cudaError_t launch_pull_rows(const void* const* peers, int n_peers, int64_t peer_tokens,
+                             int64_t src_row_bytes, int64_t src_tensor_bytes,
+                             int64_t src_offset, const int32_t* perm, int64_t tokens,
+                             int64_t row_bytes, void* const* dst, int* err_word,
+                             cudaStream_t stream, int num_sms);
 
 // ---- (b) route selection / CSR pack ----------------------------------------
 struct SelectArgs {

@@ -365,8 +365,9 @@ class FlexReuseBackend:
         self.route_streams = {}
         self.spatial_layouts = {}
         self.pipelines = {}
-        # head_parallel on CUDA: the attention stores into the ranks' output
-        # shards over peer memory instead of an output all-to-all
+        # head_parallel on CUDA: the chunks' packed inputs are pulled from the
+        # ranks' shards and the attention stores into the ranks' output shards
+        # over peer memory, instead of NCCL all-to-alls
         self.peer_exchange = True
         self.log = PhaseLog()
 
@@ -744,7 +745,8 @@ class FlexReuseBackend:
             inverse = layout.inverse_cpu if layout is not None else None
             pipe = parallel.PipelinedHeadParallel(group, group_size, heads, q.shape[1], perm,
                                                   inverse, chunks=chunks, rows=rows,
-                                                  peer_out=self.peer_exchange and q.is_cuda)
+                                                  peer_out=self.peer_exchange and q.is_cuda,
+                                                  peer_in=self.peer_exchange and q.is_cuda)
             self.pipelines[pkey] = pipe
         counts, indices = state.block_mask.counts[0], state.block_mask.indices[0]
         hc = pipe.hc

@@ -635,3 +635,25 @@ def ipc_import(handle: bytes, offset: int) -> int:
 
 def ipc_release(ptr: int, offset: int) -> None:
     _native.call("bsa_ipc_release", int(ptr), int(offset))
+
+
+def pull_rows(peer_shards: Sequence[int], peer_tokens: int, src_row_bytes: int,
+              src_tensor_bytes: int, src_offset: int, dst: Sequence[torch.Tensor],
+              perm: torch.Tensor | None = None) -> None:
+    """Pull the packed rows of this call's heads from the ranks' input shards
+    (``bsa_pull_rows``): ``dst[x][0, i]`` (``x`` = Q, K, V; ``[1, T, h, D]``
+    contiguous) = ``row_bytes`` bytes of token ``t = perm[i]`` from rank
+    ``t // peer_tokens``'s shard ``peer_shards[p]`` (device pointers)."""
+    device = _require_cuda(*dst)
+    if len(dst) != 3 or any(not d.is_contiguous() for d in dst):
+        raise ValueError("dst must be three contiguous tensors")
+    T = dst[0].shape[1]
+    row_bytes = dst[0][0, 0].numel() * dst[0].element_size()
+    if perm is not None and (perm.dtype != torch.int32 or perm.shape != (T,)
+                             or perm.device != device):
+        raise ValueError("perm must be int32 [T] on dst's device")
+    arr = (ctypes.c_void_p * len(peer_shards))(*[int(p) for p in peer_shards])
+    outs = (ctypes.c_void_p * 3)(*[d.data_ptr() for d in dst])
+    _native.call("bsa_pull_rows", arr, len(peer_shards), int(peer_tokens), int(src_row_bytes),
+                 int(src_tensor_bytes), int(src_offset), _native.ptr(perm), T, row_bytes, outs,
+                 _native.err_word(device).data_ptr(), _stream(device))

@@ -298,10 +298,18 @@ class PipelinedHeadParallel:
     the shard is read.  The next call's first input exchange cannot complete
     before every rank has started that call, so no rank stores into a shard
     its owner is still reading.
+    
+    ``peer_in`` (with ``peer_out``): no input all-to-all either.  Every rank's
+    Q/K/V shard sits in a mapped buffer (``input_buffers``; other inputs are
+    copied there), and each chunk's packed rows are pulled from the ranks'
+    shards over peer memory (``kernels.pull_rows``) on a high-priority side
+    stream while earlier chunks attend.  One all-reduce before the pulls
+    (every shard written) and one after the attention (every store done)
+    are the only collectives.
     """
 
     def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
-                 chunks=None, rows=None, peer_out=False):
+                 chunks=None, rows=None, peer_out=False, peer_in=False):
         if heads % group_size:
             raise ValueError(f"{heads} heads do not split over {group_size} ranks")
         self.group = group
@@ -335,13 +343,96 @@ class PipelinedHeadParallel:
         self.tables = _Tables(builders)
         self.rows = rows or CudaRows
         self.peer_out = peer_out
+        self.peer_in = peer_in and peer_out
         self.peer_error = None
         self._shards = {}
+        self._in_shards = {}
+        self._pull = {}
+
+    def input_buffers(self, device, dtype, head_dim):
+        """With ``peer_in``: (q, k, v) ``[1, T/P, H, D]`` views of this rank's
+        mapped input shard; inputs written there are not copied by the call."""
+        ins = self._input_shards(torch.device(device), dtype, self.hp * self.P, head_dim)
+        return tuple(ins.local[x][None] for x in range(3))
+
+    def _input_shards(self, device, dtype, h, d):
+        key = (device, dtype, d)
+        ins = self._in_shards.get(key)
+        if ins is None:
+            ins = self._in_shards[key] = PeerShards(self.group, self.P, (3, self.tl, h, d),
+                                                    dtype, device)
+        return ins
+
+    def _output_shards(self, device, dtype, h, d):
+        key = (device, dtype)
+        shards = self._shards.get(key)
+        if shards is None:
+            shards = self._shards[key] = PeerShards(self.group, self.P, (self.tl, h, d), dtype,
+                                                    device)
+        return shards
+
+    def _pull_call(self, q, k, v, attend):
+        """Input exchange by pulls over peer memory, output by the attention's
+        stores: no NCCL all-to-all.  The caller's shards go into this rank's
+        mapped input shard (unless already there); after one all-reduce every
+        rank's inputs are in place, and a high-priority side stream pulls each
+        chunk's packed rows (``kernels.pull_rows``) while earlier chunks
+        attend."""
+        from . import kernels
+        from .kernels import PeerRows
+        _, tl, h, d = q.shape
+        dev = q.device
+        ins = self._input_shards(dev, q.dtype, h, d)
+        outs = self._output_shards(dev, q.dtype, h, d)
+        if not (ins.ready and outs.ready):
+            self.peer_in = self.peer_out = False
+            self.peer_error = ins.error or outs.error
+            return None
+        for x, t in enumerate((q, k, v)):
+            if t.data_ptr() != ins.local[x].data_ptr():
+                ins.local[x].copy_(t[0])
+        # every rank's inputs are in its shard before any rank pulls
+        joined = torch.zeros(1, dtype=torch.float32, device=dev)
+        dist.all_reduce(joined, group=self.group)
+        state = self._pull.get(dev)
+        if state is None:
+            side = torch.cuda.Stream(device=dev, priority=-1)
+            bufs = [[torch.empty((1, tl * self.P, self.hc, d), dtype=q.dtype, device=dev)
+                     for _ in range(3)] for _ in range(self.chunks)]
+            state = self._pull[dev] = (side, bufs)
+        side, bufs = state
+        cur = torch.cuda.current_stream(dev)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        side.wait_event(ready)
+        me = dist.get_rank(self.group)
+        perm = self.tables.get("perm", dev) if self.has_perm else None
+        pulled = []
+        with torch.cuda.stream(side):
+            for c in range(self.chunks):
+                kernels.pull_rows(ins.ptrs, tl, h * d * q.element_size(),
+                                  tl * h * d * q.element_size(),
+                                  (me * self.hp + c * self.hc) * d * q.element_size(), bufs[c],
+                                  perm)
+                e = torch.cuda.Event()
+                e.record(side)
+                pulled.append(e)
+        mine = PeerRows(outs.ptrs, tl, h * d, d).shifted(me * self.hp)
+        for c in range(self.chunks):
+            cur.wait_event(pulled[c])
+            attend(*bufs[c], c, None, perm, peers=mine.shifted(c * self.hc))
+        # every rank's stores into this shard are done once all ranks get here
+        dist.all_reduce(joined, group=self.group)
+        return outs.local.clone().view(1, tl, h, d)
 
     def __call__(self, q, k, v, attend):
         b, tl, h, d = q.shape
         if b != 1 or tl != self.tl or h != self.hp * self.P:
             raise ValueError("PipelinedHeadParallel takes [1, T/P, H, D] shards of one branch")
+        if self.peer_in:
+            out = self._pull_call(q, k, v, attend)
+            if out is not None:
+                return out
         P, hc, C = self.P, self.hc, self.chunks
         T = P * tl
         dev = q.device
@@ -388,11 +479,7 @@ class PipelinedHeadParallel:
     def _peer_call(self, q, recv, inputs, attend, out_rows, span):
         from .kernels import PeerRows
         _, tl, h, d = q.shape
-        key = (q.device, q.dtype)
-        shards = self._shards.get(key)
-        if shards is None:
-            shards = self._shards[key] = PeerShards(self.group, self.P, (tl, h, d), q.dtype,
-                                                    q.device)
+        shards = self._output_shards(q.device, q.dtype, h, d)
         if not shards.ready:
             # some rank could not map the shards: every rank exchanges by NCCL
             self.peer_out = False

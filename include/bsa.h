@@ -347,6 +347,25 @@ BSA_API int bsa_attention_fwd_peers(const void* q, const void* k, const void* v,
                                     int64_t out_stride_h, int32_t* err_word, void* stream);
 
 /*
+ * (e) The input side of the head-parallel exchange as pulls over peer
+ * memory: for every packed row i (token t = perm[i], or i when perm is NULL)
+ * and each of Q, K, V (x = 0, 1, 2), row_bytes bytes are read from rank
+ * p = t / peer_tokens's input shard peer_shards[p] at byte
+ * x * src_tensor_bytes + (t - p * peer_tokens) * src_row_bytes + src_offset
+ * and written to dst[x] + i * row_bytes.  A shard is [3, peer_tokens, H, D]
+ * (Q, K, V of the rank's tokens, every head); src_offset selects this rank's
+ * heads.  peer_shards[p] is rank p's shard mapped into this process
+ * (bsa_ipc_import; this rank's own for p = its rank), n_peers <= 8, all
+ * sizes and addresses 16-byte multiples.  The caller joins the ranks (a
+ * collective) after writing its shard and before any rank pulls.  No
+ * reference counterpart: it replaces an all-to-all plus the pack gather.
+ */
+BSA_API int bsa_pull_rows(const void* const* peer_shards, int32_t n_peers, int64_t peer_tokens,
+                          int64_t src_row_bytes, int64_t src_tensor_bytes, int64_t src_offset,
+                          const int32_t* perm, int64_t tokens, int64_t row_bytes,
+                          void* const* dst, int32_t* err_word, void* stream);
+
+/*
  * (e) CUDA IPC of a device buffer between the processes of a head-parallel
  * group.  bsa_ipc_export writes the 64-byte handle of the allocation holding
  * ptr and ptr's offset in it; bsa_ipc_import maps a handle exported by

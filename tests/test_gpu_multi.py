@@ -3,7 +3,8 @@
 Two ranks hold sequence shards of one branch; every exchange path - the
 unchunked ``head_parallel_attention``, the chunked ``PipelinedHeadParallel``
 with the routed kernel storing into the output all-to-all's send buffer or
-straight into the ranks' output shards over peer memory (twice in a row), and
+straight into the ranks' output shards over peer memory (twice in a row),
+with the inputs pulled from the ranks' mapped shards as well, and
 the public ``FlexReuseBackend.head_parallel`` on a reuse call - must give the
 single-GPU result on every row of the rank's shard.  Skipped with fewer than two GPUs; the host-side
 layout logic is covered on CPU by tests/test_parallel_gloo.py.
@@ -87,13 +88,25 @@ def _worker(rank, world, port, queue):
         # the output exchange inside the attention: stores into the ranks'
         # shards over peer memory, twice in a row (the second call stores into
         # shards the first call's owners have read)
-        pipe_p = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
+        pipe_o = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
                                                 perm=lay.permutation_cpu,
                                                 inverse=lay.inverse_cpu, chunks=2, peer_out=True)
         shard = [x[:, sl].contiguous() for x in (q, k, v)]
-        out4 = pipe_p(*shard, attend_chunk)
-        out5 = pipe_p(*[x.flip(1).contiguous() for x in shard], attend_chunk)
-        out4b = pipe_p(*shard, attend_chunk)
+        out4 = pipe_o(*shard, attend_chunk)
+        out5 = pipe_o(*[x.flip(1).contiguous() for x in shard], attend_chunk)
+        out4b = pipe_o(*shard, attend_chunk)
+        # and the input exchange as pulls from the ranks' mapped input shards:
+        # copied in, then already in place
+        pipe_p = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
+                                                perm=lay.permutation_cpu,
+                                                inverse=lay.inverse_cpu, chunks=2, peer_out=True,
+                                                peer_in=True)
+        out6 = pipe_p(*shard, attend_chunk)
+        bufs = pipe_p.input_buffers(dev, q.dtype, 128)
+        for dst_t, src_t in zip(bufs, shard):
+            dst_t.copy_(src_t)
+        out7 = pipe_p(*bufs, attend_chunk)
+        assert pipe_p.peer_in and pipe_o.peer_out and not pipe_o.peer_in
         # the public API: FlexReuseBackend.head_parallel on a reuse call
         backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True))
         backend.install_route(route[hs].to(dev), attention_id=1, branch=0, tokens=T, heads=hp,
@@ -108,6 +121,8 @@ def _worker(rank, world, port, queue):
         errs.append(float((out3.float() - ref[:, sl].float()).abs().max()))
         errs.append(float((out4.float() - ref[:, sl].float()).abs().max()))
         errs.append(float((out4b.float() - ref[:, sl].float()).abs().max()))
+        errs.append(float((out6.float() - ref[:, sl].float()).abs().max()))
+        errs.append(float((out7.float() - ref[:, sl].float()).abs().max()))
         assert not torch.equal(out5, out4)
         assert backend.pipelines and all(p.peer_out for p in backend.pipelines.values())
         queue.put((rank, errs))
@@ -132,4 +147,4 @@ def test_exchange_paths_match_single_gpu():
     for rank, errs in results.items():
         assert not isinstance(errs, str), errs
         # the same kernels on the same rows: the exchange must not change a bit
-        assert errs == [0.0] * 5, (rank, errs)
+        assert errs == [0.0] * 7, (rank, errs)
