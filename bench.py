@@ -496,7 +496,6 @@ def main(argv=None):
                                               inverse=layout.inverse_cpu,
                                               peer_out=args.exchange == "peer",
                                               peer_in=args.exchange == "peer")
-        hc = pipe.hc
         if pipe.peer_in and len(branches) == 1:
             # the step's inputs live in this rank's mapped input shard (as a
             # caller that produces them there would have them): no copy
@@ -504,9 +503,16 @@ def main(argv=None):
             for dst_t, src_t in zip(bufs, (q, k, v)):
                 dst_t.copy_(src_t)
             q, k, v = bufs
-        chunk_csr = [[(counts[bi, c * hc:(c + 1) * hc].contiguous(),
-                       indices[bi, c * hc:(c + 1) * hc].contiguous())
-                      for c in range(pipe.chunks)] for bi in range(len(branches))]
+        csr_cache = {}
+
+        def chunk_csr(bi, c):
+            # the CSR rows of chunk c's heads (the chunk plan of the exchange
+            # in effect), cut once per branch and chunk
+            hs = pipe.chunk_slices()[c]
+            key = (bi, hs.start, hs.stop)
+            if key not in csr_cache:
+                csr_cache[key] = (counts[bi, hs].contiguous(), indices[bi, hs].contiguous())
+            return csr_cache[key]
         branch_now = [0]
 
         chunk_events = []
@@ -518,7 +524,7 @@ def main(argv=None):
             cur = torch.cuda.current_stream(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(cur)
-            csr = chunk_csr[branch_now[0]][c]
+            csr = chunk_csr(branch_now[0], c)
             if peers is not None:
                 kernels.block_sparse_attention_peers(qp, kp, vp, *csr, peers, block=cfg.block,
                                                      out_rows=out_rows)
@@ -527,7 +533,7 @@ def main(argv=None):
                                                out_rows=out_rows)
             e1.record(cur)
             chunk_events.append((e0, e1))
-            if c == pipe.chunks - 1:
+            if c == len(pipe.chunk_slices()) - 1:
                 # attention time of the step: first chunk start to last chunk end
                 attn_events.append((chunk_events[0][0], [e for _, e in chunk_events]))
                 chunk_events.clear()
@@ -658,7 +664,9 @@ def main(argv=None):
             * cfg.batch / (ms * 1e-3) / 1e12,
             "parallelism": ("single GPU" if world == 1 else
                             f"{plan.cfg_groups} CFG group(s) x {P}-way head parallel "
-                            + (f"({pipe.chunks} head chunks overlapped with attention; "
+                            + (f"({len(pipe.chunk_slices())} head chunks "
+                               f"({[sl.stop - sl.start for sl in pipe.chunk_slices()]} heads) "
+                               "overlapped with attention; "
                                + ("inputs pulled from the ranks' shards and outputs stored by "
                                   "the attention into them, over peer memory)"
                                   if pipe.peer_in else
@@ -674,7 +682,8 @@ def main(argv=None):
         # per rank and branch: C send-row scatters, C receive gathers, C
         # attentions (+ C output scatters with the NCCL output all-to-all)
         "gpu_launches": args.steps * world * (
-            len(branches) * pipe.chunks * (2 if pipe.peer_in else 3 if pipe.peer_out else 4)
+            len(branches) * len(pipe.chunk_slices())
+            * (2 if pipe.peer_in else 3 if pipe.peer_out else 4)
             if pipe is not None else 2),
         **({"rank_ms": rank_ms} if rank_ms is not None else {}),
         "clocks": clocks.summary(),

@@ -749,11 +749,10 @@ class FlexReuseBackend:
                                                   peer_in=self.peer_exchange and q.is_cuda)
             self.pipelines[pkey] = pipe
         counts, indices = state.block_mask.counts[0], state.block_mask.indices[0]
-        hc = pipe.hc
         scale = call_kw.get("softmax_scale")
 
         def attend(qp, kp, vp, chunk, out, out_rows, peers=None):
-            hs = slice(chunk * hc, (chunk + 1) * hc)
+            hs = pipe.chunk_slices()[chunk]     # the plan of the exchange in effect
             if peers is not None:
                 kernels.block_sparse_attention_peers(qp, kp, vp, counts[hs], indices[hs], peers,
                                                      block=self.config.block_size, scale=scale,

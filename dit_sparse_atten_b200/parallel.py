@@ -309,7 +309,7 @@ class PipelinedHeadParallel:
     """
 
     def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
-                 chunks=None, rows=None, peer_out=False, peer_in=False):
+                 chunks=None, rows=None, peer_out=False, peer_in=False, pull_chunks=None):
         if heads % group_size:
             raise ValueError(f"{heads} heads do not split over {group_size} ranks")
         self.group = group
@@ -344,10 +344,29 @@ class PipelinedHeadParallel:
         self.rows = rows or CudaRows
         self.peer_out = peer_out
         self.peer_in = peer_in and peer_out
+        # Pull mode cuts the heads freely (no all-to-all layout): a small
+        # first chunk, whose pull is the only one not hidden under an
+        # attention, then the rest in one launch.
+        if pull_chunks is None:
+            first = max(1, self.hp // 5)
+            pull_chunks = [first, self.hp - first] if self.hp > first else [self.hp]
+        if sum(pull_chunks) != self.hp or min(pull_chunks) < 1:
+            raise ValueError("pull_chunks must be positive head counts summing to the rank's heads")
+        self.pull_chunks = list(pull_chunks)
         self.peer_error = None
         self._shards = {}
         self._in_shards = {}
         self._pull = {}
+
+    def chunk_slices(self):
+        """This rank's local head range of every chunk, in call order, for the
+        exchange in effect (pull chunks with ``peer_in``, else equal ones)."""
+        sizes = self.pull_chunks if self.peer_in else [self.hc] * self.chunks
+        out, start = [], 0
+        for n in sizes:
+            out.append(slice(start, start + n))
+            start += n
+        return out
 
     def input_buffers(self, device, dtype, head_dim):
         """With ``peer_in``: (q, k, v) ``[1, T/P, H, D]`` views of this rank's
@@ -394,11 +413,12 @@ class PipelinedHeadParallel:
         # every rank's inputs are in its shard before any rank pulls
         joined = torch.zeros(1, dtype=torch.float32, device=dev)
         dist.all_reduce(joined, group=self.group)
+        slices = self.chunk_slices()
         state = self._pull.get(dev)
         if state is None:
             side = torch.cuda.Stream(device=dev, priority=-1)
-            bufs = [[torch.empty((1, tl * self.P, self.hc, d), dtype=q.dtype, device=dev)
-                     for _ in range(3)] for _ in range(self.chunks)]
+            bufs = [[torch.empty((1, tl * self.P, sl.stop - sl.start, d), dtype=q.dtype,
+                                 device=dev) for _ in range(3)] for sl in slices]
             state = self._pull[dev] = (side, bufs)
         side, bufs = state
         cur = torch.cuda.current_stream(dev)
@@ -409,18 +429,18 @@ class PipelinedHeadParallel:
         perm = self.tables.get("perm", dev) if self.has_perm else None
         pulled = []
         with torch.cuda.stream(side):
-            for c in range(self.chunks):
+            for c, sl in enumerate(slices):
                 kernels.pull_rows(ins.ptrs, tl, h * d * q.element_size(),
                                   tl * h * d * q.element_size(),
-                                  (me * self.hp + c * self.hc) * d * q.element_size(), bufs[c],
+                                  (me * self.hp + sl.start) * d * q.element_size(), bufs[c],
                                   perm)
                 e = torch.cuda.Event()
                 e.record(side)
                 pulled.append(e)
         mine = PeerRows(outs.ptrs, tl, h * d, d).shifted(me * self.hp)
-        for c in range(self.chunks):
+        for c, sl in enumerate(slices):
             cur.wait_event(pulled[c])
-            attend(*bufs[c], c, None, perm, peers=mine.shifted(c * self.hc))
+            attend(*bufs[c], c, None, perm, peers=mine.shifted(sl.start))
         # every rank's stores into this shard are done once all ranks get here
         dist.all_reduce(joined, group=self.group)
         return outs.local.clone().view(1, tl, h, d)

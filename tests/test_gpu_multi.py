@@ -71,20 +71,23 @@ def _worker(rank, world, port, queue):
         pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
                                               perm=lay.permutation_cpu, inverse=lay.inverse_cpu,
                                               chunks=2)
-        hc = pipe.hc
 
-        def attend_chunk(qp_, kp_, vp_, c, out_c, out_rows, peers=None):
-            cs = slice(c * hc, (c + 1) * hc)
-            if peers is not None:
-                kernels.block_sparse_attention_peers(qp_, kp_, vp_, c_loc[cs].contiguous(),
-                                                     i_loc[cs].contiguous(), peers,
-                                                     out_rows=out_rows)
-                return
-            kernels.block_sparse_attention(qp_, kp_, vp_, c_loc[cs].contiguous(),
-                                           i_loc[cs].contiguous(), out=out_c, out_rows=out_rows)
+        def attend_for(pipe_):
+            # chunk c's local heads under the chunk plan of pipe_'s exchange
+            def attend_chunk(qp_, kp_, vp_, c, out_c, out_rows, peers=None):
+                cs = pipe_.chunk_slices()[c]
+                if peers is not None:
+                    kernels.block_sparse_attention_peers(qp_, kp_, vp_, c_loc[cs].contiguous(),
+                                                         i_loc[cs].contiguous(), peers,
+                                                         out_rows=out_rows)
+                    return
+                kernels.block_sparse_attention(qp_, kp_, vp_, c_loc[cs].contiguous(),
+                                               i_loc[cs].contiguous(), out=out_c,
+                                               out_rows=out_rows)
+            return attend_chunk
 
         out2 = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(),
-                    attend_chunk)
+                    attend_for(pipe))
         # the output exchange inside the attention: stores into the ranks'
         # shards over peer memory, twice in a row (the second call stores into
         # shards the first call's owners have read)
@@ -92,20 +95,22 @@ def _worker(rank, world, port, queue):
                                                 perm=lay.permutation_cpu,
                                                 inverse=lay.inverse_cpu, chunks=2, peer_out=True)
         shard = [x[:, sl].contiguous() for x in (q, k, v)]
-        out4 = pipe_o(*shard, attend_chunk)
-        out5 = pipe_o(*[x.flip(1).contiguous() for x in shard], attend_chunk)
-        out4b = pipe_o(*shard, attend_chunk)
+        out4 = pipe_o(*shard, attend_for(pipe_o))
+        out5 = pipe_o(*[x.flip(1).contiguous() for x in shard], attend_for(pipe_o))
+        out4b = pipe_o(*shard, attend_for(pipe_o))
         # and the input exchange as pulls from the ranks' mapped input shards:
         # copied in, then already in place
         pipe_p = parallel.PipelinedHeadParallel(dist.group.WORLD, world, H, tl,
                                                 perm=lay.permutation_cpu,
                                                 inverse=lay.inverse_cpu, chunks=2, peer_out=True,
                                                 peer_in=True)
-        out6 = pipe_p(*shard, attend_chunk)
+        # pulls are cut unevenly: a one-head first chunk, then the rest
+        assert [s_.stop - s_.start for s_ in pipe_p.chunk_slices()] == [1, hp - 1]
+        out6 = pipe_p(*shard, attend_for(pipe_p))
         bufs = pipe_p.input_buffers(dev, q.dtype, 128)
         for dst_t, src_t in zip(bufs, shard):
             dst_t.copy_(src_t)
-        out7 = pipe_p(*bufs, attend_chunk)
+        out7 = pipe_p(*bufs, attend_for(pipe_p))
         assert pipe_p.peer_in and pipe_o.peer_out and not pipe_o.peer_in
         # the public API: FlexReuseBackend.head_parallel on a reuse call
         backend = FlexReuseBackend(FlexReuseConfig(spatial_reorder=True))

@@ -253,6 +253,31 @@ def test_pipeline_chunk_rule():
         parallel.PipelinedHeadParallel(None, 2, 40, 16, perm=torch.arange(32))
 
 
+def test_pipeline_chunk_plans():
+    """Equal chunks for the all-to-all exchanges; the pull exchange cuts a
+    small first chunk (its pull is the one not hidden under an attention)
+    and attends the rest in one launch."""
+    def plan(pipe):
+        return [(s.start, s.stop) for s in pipe.chunk_slices()]
+    assert plan(parallel.PipelinedHeadParallel(None, 2, 20, 16, chunks=2)) == [(0, 5), (5, 10)]
+    assert plan(parallel.PipelinedHeadParallel(None, 2, 20, 16, chunks=2, peer_out=True)) == \
+        [(0, 5), (5, 10)]
+    assert plan(parallel.PipelinedHeadParallel(None, 2, 20, 16, chunks=2, peer_out=True,
+                                               peer_in=True)) == [(0, 2), (2, 10)]
+    assert plan(parallel.PipelinedHeadParallel(None, 8, 40, 16, peer_out=True,
+                                               peer_in=True)) == [(0, 1), (1, 5)]
+    assert plan(parallel.PipelinedHeadParallel(None, 2, 40, 16, peer_out=True, peer_in=True,
+                                               pull_chunks=[4, 8, 8])) == [(0, 4), (4, 12),
+                                                                           (12, 20)]
+    # pull chunks without peer outputs do not apply
+    assert plan(parallel.PipelinedHeadParallel(None, 2, 20, 16, chunks=2, peer_in=True)) == \
+        [(0, 5), (5, 10)]
+    for bad in ([3, 3], [0, 10], [11, -1]):
+        with pytest.raises(ValueError):
+            parallel.PipelinedHeadParallel(None, 2, 20, 16, peer_out=True, peer_in=True,
+                                           pull_chunks=bad)
+
+
 def test_keep_fraction_is_global():
     results = run_ranks(_keep)
     assert results[0] == results[1] == pytest.approx(16 / 64)
