@@ -222,6 +222,54 @@ def _backend_head_parallel(rank, world):
     return True
 
 
+def _peer_fallback(rank, world):
+    """Peer exchange set-up failing on one rank: every rank learns it from the
+    group (a MIN all-reduce), and the pipelined call takes the all-to-all
+    exchange with equal chunks instead, output unchanged.  The CUDA IPC calls
+    are replaced by host fakes; no device memory is mapped."""
+    from dit_sparse_atten_b200 import kernels
+
+    def export(t):
+        if rank == 1:
+            raise RuntimeError("cannot export this allocation")
+        return bytes(range(64)), 256
+    kernels.ipc_export = export
+    kernels.ipc_import = lambda handle, device: 1 << 20
+    shards = parallel.PeerShards(dist.group.WORLD, world, (4, 2, 8), torch.float32, "cpu")
+    assert not shards.ready
+    assert (shards.error is not None) == (rank == 1)
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((1, 32, 10, 8), generator=g) for _ in range(3))
+    t = q.shape[1] // world
+    sl = slice(rank * t, (rank + 1) * t)
+    perm = torch.randperm(q.shape[1], generator=torch.Generator().manual_seed(6))
+    inverse = torch.empty_like(perm)
+    inverse[perm] = torch.arange(perm.numel())
+
+    def attend(qp, kp, vp, chunk, out, out_rows, peers=None):
+        assert peers is None, "no peer stores after a failed set-up"
+        return torch.nn.functional.scaled_dot_product_attention(
+            qp.transpose(1, 2), kp.transpose(1, 2), vp.transpose(1, 2)).transpose(1, 2)
+
+    pipe = parallel.PipelinedHeadParallel(dist.group.WORLD, world, 10, t, perm=perm,
+                                          inverse=inverse, chunks=5, rows=CpuRows,
+                                          peer_out=True, peer_in=True)
+    assert [(s.start, s.stop) for s in pipe.chunk_slices()] == [(0, 1), (1, 5)]
+    out = pipe(q[:, sl].contiguous(), k[:, sl].contiguous(), v[:, sl].contiguous(), attend)
+    ref = attend(q, k, v, 0, None, None)[:, sl]
+    torch.testing.assert_close(out, ref)
+    assert not pipe.peer_in and not pipe.peer_out
+    assert (pipe.peer_error is not None) == (rank == 1)
+    assert [(s.start, s.stop) for s in pipe.chunk_slices()] == [(c, c + 1) for c in range(5)]
+    # every rank exports: the shards are mapped, this rank's own by address
+    kernels.ipc_export = lambda t: (bytes(range(64)), 256)
+    shards = parallel.PeerShards(dist.group.WORLD, world, (4, 2, 8), torch.float32, "cpu")
+    assert shards.ready and shards.error is None
+    assert shards.ptrs[rank] == shards.local.data_ptr()
+    assert shards.ptrs[1 - rank] == (1 << 20) + 256
+    return True
+
+
 def _keep(rank, world):
     from dit_sparse_atten_b200.flex import FlexReuseBackend
     backend = FlexReuseBackend(process_group=dist.group.WORLD)
@@ -243,6 +291,10 @@ def test_pipelined_exchange_equals_full_attention():
 
 def test_backend_head_parallel_pipelines_reuse_calls():
     assert all(run_ranks(_backend_head_parallel).values())
+
+
+def test_peer_exchange_falls_back_on_every_rank():
+    assert all(run_ranks(_peer_fallback).values())
 
 
 def test_pipeline_chunk_rule():
