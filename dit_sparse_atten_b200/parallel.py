@@ -212,10 +212,13 @@ _IPC_BASES: dict = {}
 
 
 class PeerShards:
-    """This rank's output shard ``[T/P, H, D]`` and every group rank's shard
-    mapped into this process (CUDA IPC, exchanged once over the group), so an
-    attention kernel can store each output row into the rank that holds its
-    token.  ``ptrs[d]`` is rank d's shard (this rank's own for d = its rank)."""
+    """This rank's shard (``shape``: the output ``[T/P, H, D]``, or the
+    inputs ``[3, T/P, H, D]``) and every group rank's shard mapped into this
+    process (CUDA IPC, exchanged once over the group), so a kernel can store
+    each output row into the rank that holds its token, or pull each input
+    row from it.  ``ptrs[d]`` is rank d's shard (this rank's own for d = its
+    rank).  ``ready`` is the same on every rank: False when any rank could
+    not export or map a shard (``error`` holds this rank's cause, if any)."""
 
     def __init__(self, group, group_size, shape, dtype, device):
         from . import kernels
@@ -298,14 +301,19 @@ class PipelinedHeadParallel:
     the shard is read.  The next call's first input exchange cannot complete
     before every rank has started that call, so no rank stores into a shard
     its owner is still reading.
-    
+
     ``peer_in`` (with ``peer_out``): no input all-to-all either.  Every rank's
     Q/K/V shard sits in a mapped buffer (``input_buffers``; other inputs are
     copied there), and each chunk's packed rows are pulled from the ranks'
     shards over peer memory (``kernels.pull_rows``) on a high-priority side
     stream while earlier chunks attend.  One all-reduce before the pulls
     (every shard written) and one after the attention (every store done)
-    are the only collectives.
+    are the only collectives.  Pull chunks need no all-to-all layout, so
+    they are cut by ``pull_chunks`` (head counts; default a fifth of the
+    rank's heads, at least one, then the rest): only the first chunk's pull
+    waits in front of an attention.  ``chunk_slices()`` gives the local head
+    range of every chunk of the exchange in effect.  If any rank cannot map
+    the shards, every rank takes the all-to-all exchange (equal chunks).
     """
 
     def __init__(self, group, group_size, heads, tokens_local, perm=None, inverse=None,
