@@ -61,6 +61,9 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cfg-split", action="store_true",
                    help="one rank group for both CFG branches (every rank exchanges heads)")
+    p.add_argument("--pull-chunks", default=None,
+                   help="N > 2 with --exchange peer: head counts of the pull chunks, "
+                        "comma-separated (default: a fifth of the rank's heads, then the rest)")
     p.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                    help="N > 2: head exchange over peer memory (inputs pulled from the ranks' "
                         "shards, outputs stored by the attention into them), or by NCCL "
@@ -495,7 +498,10 @@ def main(argv=None):
                                               perm=layout.permutation_cpu,
                                               inverse=layout.inverse_cpu,
                                               peer_out=args.exchange == "peer",
-                                              peer_in=args.exchange == "peer")
+                                              peer_in=args.exchange == "peer",
+                                              pull_chunks=([int(x) for x in
+                                                            args.pull_chunks.split(",")]
+                                                           if args.pull_chunks else None))
         if pipe.peer_in and len(branches) == 1:
             # the step's inputs live in this rank's mapped input shard (as a
             # caller that produces them there would have them): no copy
