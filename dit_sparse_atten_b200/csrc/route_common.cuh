@@ -26,83 +26,107 @@ __device__ __forceinline__ int ceil_log2(int v) {
   return v <= 1 ? 0 : 32 - __clz(v - 1);
 }
 
-// Cascade over `size` items; item i of this lane is load(index(i)).  Items
-// are loaded kBatch at a time ahead of their in-order additions.
+// The ordered sums below run on float (one sum) or float2 (two sums of the
+// same length in one packed chain: each component is added exactly as a
+// float sum would be).
+__device__ __forceinline__ float sum_add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float2 sum_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+template <typename T>
+__device__ __forceinline__ T sum_zero() {
+  if constexpr (sizeof(T) == sizeof(float)) {
+    return 0.f;
+  } else {
+    return make_float2(0.f, 0.f);
+  }
+}
+__device__ __forceinline__ float sum_shfl(float v, int src) {
+  return __shfl_sync(0xffffffffu, v, src);
+}
+__device__ __forceinline__ float2 sum_shfl(float2 v, int src) {
+  return make_float2(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src));
+}
+
+// Cascade over `size` items; item i of this lane is load(index(i)) (a float,
+// or a float2 for two sums at once).  Items are loaded kBatch at a time ahead
+// of their in-order additions.
 template <int kBatch = 8, typename Load, typename IndexFn>
-__device__ float cascade_sum(Load load, int size, IndexFn index) {
+__device__ auto cascade_sum(Load load, int size, IndexFn index) {
+  using T = decltype(load(0));
   static_assert(kBatch == 8 || kBatch == 16, "level_step is a multiple of 16");
   const int level_power = max(4, ceil_log2(size) / 4);
   const int level_step = 1 << level_power;
   const int level_mask = level_step - 1;
-  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  T acc0 = sum_zero<T>(), acc1 = sum_zero<T>(), acc2 = sum_zero<T>(), acc3 = sum_zero<T>();
   int i = 0;
   while (i + level_step <= size) {
     // level_step is a power of two >= 16: items go in groups of kBatch, all
     // loaded before any is added (the additions keep their order).
     for (int j = 0; j < level_step; j += kBatch, i += kBatch) {
-      float x[kBatch];
+      T x[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) x[u] = load(index(i + u));
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) acc0 = __fadd_rn(acc0, x[u]);
+      for (int u = 0; u < kBatch; ++u) acc0 = sum_add(acc0, x[u]);
     }
-    acc1 = __fadd_rn(acc1, acc0);
-    acc0 = 0.f;
+    acc1 = sum_add(acc1, acc0);
+    acc0 = sum_zero<T>();
     if ((i & (level_mask << level_power)) != 0) continue;
-    acc2 = __fadd_rn(acc2, acc1);
-    acc1 = 0.f;
+    acc2 = sum_add(acc2, acc1);
+    acc1 = sum_zero<T>();
     if ((i & (level_mask << (2 * level_power))) != 0) continue;
-    acc3 = __fadd_rn(acc3, acc2);
-    acc2 = 0.f;
+    acc3 = sum_add(acc3, acc2);
+    acc2 = sum_zero<T>();
   }
-  for (; i < size; ++i) acc0 = __fadd_rn(acc0, load(index(i)));
-  acc0 = __fadd_rn(acc0, acc1);
-  acc0 = __fadd_rn(acc0, acc2);
-  acc0 = __fadd_rn(acc0, acc3);
+  for (; i < size; ++i) acc0 = sum_add(acc0, load(index(i)));
+  acc0 = sum_add(acc0, acc1);
+  acc0 = sum_add(acc0, acc2);
+  acc0 = sum_add(acc0, acc3);
   return acc0;
 }
 
 // float32 sum of load(0..n-1) in the reference's CPU order (ATen's vectorised
 // cascade: lane (k, v) of 4 accumulators x 8 float lanes takes items
 // (4 i + k) * 8 + v, i.e. warp lane k * 8 + v takes items 32 i + lane);
-// executed by one full warp, result valid in every lane.
+// executed by one full warp, result valid in every lane.  A load returning
+// float2 gives two such sums (of two rows of the same length) at once.
 template <int kBatch = 8, typename Load>
-__device__ float torch_cpu_sum(Load load, int n) {
+__device__ auto torch_cpu_sum(Load load, int n) {
+  using T = decltype(load(0));
   const int lane = threadIdx.x & 31;
-  float result = 0.f;
+  T result = sum_zero<T>();
   if (n < 8) {
     if (lane == 0) {
       const int size_ilp = n / 4;
-      float p[4];
+      T p[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         p[k] = cascade_sum(load, size_ilp, [k](int i) { return 4 * i + k; });
-      for (int i = size_ilp * 4; i < n; ++i) p[0] = __fadd_rn(p[0], load(i));
+      for (int i = size_ilp * 4; i < n; ++i) p[0] = sum_add(p[0], load(i));
 #pragma unroll
-      for (int k = 1; k < 4; ++k) p[0] = __fadd_rn(p[0], p[k]);
-      result = __fadd_rn(0.f, p[0]);
+      for (int k = 1; k < 4; ++k) p[0] = sum_add(p[0], p[k]);
+      result = sum_add(sum_zero<T>(), p[0]);
     }
-    return __shfl_sync(0xffffffffu, result, 0);
+    return sum_shfl(result, 0);
   }
   const int vec_size = n / 8;
   const int size_ilp = vec_size / 4;
   const int k = lane >> 3;
   const int v = lane & 7;
-  float acc = cascade_sum<kBatch>(load, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
+  T acc = cascade_sum<kBatch>(load, size_ilp, [k, v](int i) { return (4 * i + k) * 8 + v; });
   if (k == 0)
-    for (int i = size_ilp * 4; i < vec_size; ++i) acc = __fadd_rn(acc, load(i * 8 + v));
-  const float a1 = __shfl_sync(0xffffffffu, acc, (v + 8) & 31);
-  const float a2 = __shfl_sync(0xffffffffu, acc, (v + 16) & 31);
-  const float a3 = __shfl_sync(0xffffffffu, acc, (v + 24) & 31);
-  float p = __fadd_rn(__fadd_rn(__fadd_rn(acc, a1), a2), a3);
-  float f = 0.f;
+    for (int i = size_ilp * 4; i < vec_size; ++i) acc = sum_add(acc, load(i * 8 + v));
+  const T a1 = sum_shfl(acc, (v + 8) & 31);
+  const T a2 = sum_shfl(acc, (v + 16) & 31);
+  const T a3 = sum_shfl(acc, (v + 24) & 31);
+  T p = sum_add(sum_add(sum_add(acc, a1), a2), a3);
+  T f = sum_zero<T>();
   if (lane == 0)
-    for (int i = vec_size * 8; i < n; ++i) f = __fadd_rn(f, load(i));
+    for (int i = vec_size * 8; i < n; ++i) f = sum_add(f, load(i));
   for (int l = 0; l < 8; ++l) {
-    const float pl = __shfl_sync(0xffffffffu, p, l);
-    if (lane == 0) f = __fadd_rn(f, pl);
+    const T pl = sum_shfl(p, l);
+    if (lane == 0) f = sum_add(f, pl);
   }
-  return __shfl_sync(0xffffffffu, f, 0);
+  return sum_shfl(f, 0);
 }
 
 // float32 row sum of x[0..n-1] in the reference's CPU order (one full warp).

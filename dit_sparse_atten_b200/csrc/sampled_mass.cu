@@ -86,7 +86,6 @@ constexpr int kMaxDynSmem = 232448;
 // Blocks the on-chip mode holds: TMEM, then shared memory (473 at 227 KB).
 constexpr int kOnChipMaxBlocks =
     kTmemVals + (kMaxDynSmem - MassLayout<true>::kBytes) / (128 * 4);
-constexpr int kMass2Smem = MassLayout<false>::kBytes;
 constexpr int kMassEmulated = 2;  // of every 8 column pairs, exponentials on the FMA pipe
 
 // Warp layout.  S = 16, 32: sixteen softmax warps, four per SM sub-partition,
