@@ -39,3 +39,28 @@ def test_oracle_matches_reference(golden):
                                 perm=g["perm"])
     for name, got in (("q", q), ("k", k), ("v", v)):
         assert np.array_equal(got, bf16_bits_to_float(g[name])), name
+
+
+def test_rotation_products_are_exact_in_float64():
+    """The CUDA rotation rounds re*c - im*s (and re*s + im*c) once, by a fused
+    multiply-add on float64.  That equals the reference's float64 product
+    then subtraction only if every product of a bf16 value (8 significant
+    bits) and a float32 factor (24 bits) is exact in float64.  Checked here
+    with exact rationals on seeded values across the exponent range, and the
+    single rounding of the difference against the product-then-subtract."""
+    from fractions import Fraction
+    rng = np.random.default_rng(21)
+    n = 4000
+    x = (rng.standard_normal(n) * np.exp2(rng.integers(-40, 40, n))).astype(np.float32)
+    xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()          # bf16 values
+    ang = rng.uniform(-np.pi, np.pi, n)
+    c, s = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    re, im = xb[: n // 2], xb[n // 2:]
+    for a, b in ((re, c[: n // 2]), (im, s[n // 2:]), (re, s[: n // 2]), (im, c[n // 2:])):
+        for u, w in zip(a.tolist(), b.tolist()):
+            assert float(u) * float(w) == Fraction(u) * Fraction(w)
+    cc, ss = c[: n // 2].astype(np.float64), s[: n // 2].astype(np.float64)
+    for u, v, cv, sv in zip(re.tolist(), im.tolist(), cc.tolist(), ss.tolist()):
+        # one rounding of the exact difference == rounding of exact products' difference
+        exact = Fraction(u) * Fraction(cv) - Fraction(v) * Fraction(sv)
+        assert float(exact) == u * cv - v * sv
