@@ -391,7 +391,7 @@ class PipelinedHeadParallel:
         return ins
 
     def _output_shards(self, device, dtype, h, d):
-        key = (device, dtype)
+        key = (device, dtype, d)
         shards = self._shards.get(key)
         if shards is None:
             shards = self._shards[key] = PeerShards(self.group, self.P, (self.tl, h, d), dtype,
@@ -422,12 +422,13 @@ class PipelinedHeadParallel:
         joined = torch.zeros(1, dtype=torch.float32, device=dev)
         dist.all_reduce(joined, group=self.group)
         slices = self.chunk_slices()
-        state = self._pull.get(dev)
+        pull_key = (dev, q.dtype, d)     # pull buffers per device, dtype and head size
+        state = self._pull.get(pull_key)
         if state is None:
             side = torch.cuda.Stream(device=dev, priority=-1)
             bufs = [[torch.empty((1, tl * self.P, sl.stop - sl.start, d), dtype=q.dtype,
                                  device=dev) for _ in range(3)] for sl in slices]
-            state = self._pull[dev] = (side, bufs)
+            state = self._pull[pull_key] = (side, bufs)
         side, bufs = state
         cur = torch.cuda.current_stream(dev)
         ready = torch.cuda.Event()
