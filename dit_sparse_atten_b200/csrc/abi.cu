@@ -710,6 +710,9 @@ int bsa_pull_rows(const void* const* peer_shards, int32_t n_peers, int64_t peer_
       (src_offset & 15) || src_offset + row_bytes > src_row_bytes)
     return fail(BSA_ERR_INVALID_ARGUMENT, "row sizes and offsets must be 16-byte multiples "
                 "and the pulled bytes must lie inside a token's row");
+  if (src_offset < 0 || src_tensor_bytes < peer_tokens * src_row_bytes)
+    return fail(BSA_ERR_INVALID_ARGUMENT, "a shard's Q, K and V (src_tensor_bytes apart) must "
+                "not overlap: src_tensor_bytes >= peer_tokens x src_row_bytes");
   cudaError_t e = bsa::launch_pull_rows(peer_shards, n_peers, peer_tokens, src_row_bytes,
                                         src_tensor_bytes, src_offset, perm, tokens, row_bytes,
                                         dst, err_word, static_cast<cudaStream_t>(stream),

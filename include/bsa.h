@@ -356,7 +356,9 @@ BSA_API int bsa_attention_fwd_peers(const void* q, const void* k, const void* v,
  * (Q, K, V of the rank's tokens, every head); src_offset selects this rank's
  * heads.  peer_shards[p] is rank p's shard mapped into this process
  * (bsa_ipc_import; this rank's own for p = its rank), n_peers <= 8, all
- * sizes and addresses 16-byte multiples.  The caller joins the ranks (a
+ * sizes and addresses 16-byte multiples, src_offset + row_bytes <=
+ * src_row_bytes and src_tensor_bytes >= peer_tokens * src_row_bytes (else
+ * BSA_ERR_INVALID_ARGUMENT, nothing launched).  The caller joins the ranks (a
  * collective) after writing its shard and before any rank pulls.  No
  * reference counterpart: it replaces an all-to-all plus the pack gather.
  */

@@ -103,3 +103,44 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_native, "_lib", None)
     with pytest.raises(RuntimeError, match="missing"):
         _native.load_library(tmp_path / "libbsa.so")
+
+
+def test_exchange_entry_points_validate():
+    """The peer-memory exchange entry points refuse bad layouts before any
+    device work: peer counts, token splits, alignment, rows that would read
+    past a token's row or tensors that overlap."""
+    lib = _native.load_library()
+    err = ctypes.c_int32(0)
+    peers = (ctypes.c_void_p * 8)(*([4096] * 8))
+    dst = (ctypes.c_void_p * 3)(4096, 8192, 12288)
+    ok_args = dict(n_peers=2, peer_tokens=8, src_row_bytes=256, src_tensor_bytes=8 * 256,
+                   src_offset=0, tokens=16, row_bytes=128)
+
+    def pull(**kw):
+        a = {**ok_args, **kw}
+        return lib.bsa_pull_rows(peers, a["n_peers"], a["peer_tokens"], a["src_row_bytes"],
+                                 a["src_tensor_bytes"], a["src_offset"], None, a["tokens"],
+                                 a["row_bytes"], dst, ctypes.byref(err), None)
+
+    assert pull(n_peers=0) == -1 and "peers" in _err()
+    assert pull(n_peers=9, tokens=72) == -1 and "peers" in _err()
+    assert pull(tokens=15) == -1 and "tokens" in _err()
+    assert pull(row_bytes=120) == -1 and "16-byte" in _err()
+    assert pull(src_offset=160) == -1 and "inside a token's row" in _err()
+    assert pull(src_tensor_bytes=7 * 256) == -1 and "overlap" in _err()
+    assert lib.bsa_pull_rows(None, 2, 8, 256, 2048, 0, None, 16, 128, dst, ctypes.byref(err),
+                             None) == -1 and "null" in _err()
+    # attention with peer stores: peer count, token split, alignment, aliasing
+    q = 65536
+
+    def attn(out_peers, n, peer_tokens=8, tokens=16):
+        return lib.bsa_attention_fwd_peers(q, q, q, tokens, 4, 128, 512, 128, 16, 16, 1, 128,
+                                           0.1, None, out_peers, n, peer_tokens, 512, 128,
+                                           ctypes.byref(err), None)
+
+    out = (ctypes.c_void_p * 2)(4096, 8192)
+    assert attn(out, 0) == -1 and "peers" in _err()
+    assert attn(out, 9) == -1 and "peers" in _err()
+    assert attn(out, 2, peer_tokens=7) == -1 and "tokens" in _err()
+    assert attn((ctypes.c_void_p * 2)(4096, 8200), 2) == -1 and "aligned" in _err()
+    assert attn((ctypes.c_void_p * 2)(4096, q), 2) == -1 and "alias" in _err()
